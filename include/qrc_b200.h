@@ -1,0 +1,172 @@
+/*
+ * qrc_b200.h -- C ABI of the B200-native side-aware absmax library
+ * (libqrc_b200.so).
+ *
+ * The reference (QuickRunCUDA) exposes this path only through its kernel-file
+ * plugin ABI: the harness allocates A/B/C, launches `init` once and `kernel`
+ * T times, and reads C[0] (QuickRunCUDA.cpp:354-658, tests/side_aware.cu:72,
+ * :257).  The library keeps that ABI (quickruncuda_b200/csrc/side_aware_b200.cu
+ * is a drop-in kernel file) and adds these plain-C entry points so host C/C++
+ * code can call the same reduction directly.  Each entry point names the
+ * reference interface it replaces.
+ *
+ * Conventions
+ *   - All pointers named d_* are device pointers owned by the caller; h_* are
+ *     host pointers.  No function takes or returns a torch or CUDA C++ type:
+ *     streams are passed as `void*` holding a cudaStream_t (NULL = legacy
+ *     default stream).
+ *   - Every function returns QRC_OK (0) or a negative qrc_status.
+ *   - Reductions are asynchronous on the given stream unless stated.
+ *   - A context owns device scratch (the side map, its work queues and the
+ *     accumulator): at most one reduction per context may be in flight at a
+ *     time; use one context per stream or thread.
+ */
+#ifndef QRC_B200_H
+#define QRC_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct qrc_ctx qrc_ctx;
+
+enum qrc_status {
+    QRC_OK = 0,
+    QRC_ERR_INVALID = -1,   /* bad argument (NULL pointer, size, alignment) */
+    QRC_ERR_CUDA = -2,      /* a CUDA runtime call failed; see qrc_last_cuda_error() */
+    QRC_ERR_DEVICE = -3,    /* no such device, or not an sm_100 device */
+    QRC_ERR_RANGE = -4,     /* input too large for this entry point */
+    QRC_ERR_STATE = -5      /* context used with a different device */
+};
+
+/* Read modes.  SIDE_AWARE is the product path; the others exist for the
+ * ablations of the reference (tests/side_aware.cu:19-20, :305-311). */
+enum qrc_mode {
+    QRC_MODE_SIDE_AWARE = 0,        /* each side reads the chunks homed on it */
+    QRC_MODE_IGNORE_PAGE_BITS = 1,  /* FORCE_RANDOM_SIDE: page bits treated as 0 */
+    QRC_MODE_WRONG_SIDE = 2,        /* FORCE_WRONG_SIDE: every chunk read across the die boundary */
+    QRC_MODE_STREAM = 3             /* plain grid-stride stream, no side logic */
+};
+
+/* Discovery status (qrc_side_info.status). */
+enum qrc_side_status {
+    QRC_SIDE_OK = 0,
+    QRC_SIDE_TOO_SMALL = 1,         /* no full 2 MiB page inside the buffer */
+    QRC_SIDE_NO_SM_SPLIT = 2,       /* SM latencies did not form two clusters */
+    QRC_SIDE_NO_HASH = 3,           /* no address bit 4..20 changed the side */
+    QRC_SIDE_BAD_HASH = 4,          /* lowest hash bit below 512 bytes */
+    QRC_SIDE_NO_CAL_SPLIT = 5,      /* calibration words not separable */
+    QRC_SIDE_VERIFY_FAILED = 6,     /* map mispredicted > 1/8 of verification probes */
+    QRC_SIDE_TOO_MANY_PAGES = 7,    /* more pages than the map can hold */
+    QRC_SIDE_UNALIGNED = 8,         /* base not 4-byte aligned */
+    QRC_SIDE_NOT_RUN = 100          /* context created without a buffer */
+};
+
+typedef struct qrc_side_info {
+    uint32_t status;            /* qrc_side_status */
+    uint32_t mask;              /* in-page side hash mask in use (0 when not side-aware) */
+    uint32_t mask_measured;     /* mask as measured, even when rejected */
+    uint32_t chunk_bytes;       /* lowest hash bit: bytes per side chunk */
+    uint32_t num_sms_measured;
+    uint32_t sms_side0;
+    uint32_t sms_side1;
+    uint32_t num_pages;         /* 2 MiB pages spanned by the buffer */
+    uint32_t verify_probes;
+    uint32_t verify_mismatches;
+    uint32_t cal_lat_side0;     /* cycles for 32 dependent atomics, discovering SM -> side 0 word */
+    uint32_t cal_lat_side1;     /* same, side 1 word */
+    uint32_t sm_lat_cluster0;   /* phase-1 cluster means (cycles per 32 atomics) */
+    uint32_t sm_lat_cluster1;
+    uint32_t discover_smid;     /* SM that ran phase 2 */
+    uint32_t reserved;
+} qrc_side_info;
+
+/* Create a context for `device` and, when d_base != NULL, run side discovery
+ * on the device allocation [d_base, d_base + bytes): SM sides, the in-page
+ * hash mask and one side bit per 2 MiB page.  Synchronous (returns after the
+ * discovery kernel finished on `stream`).  Discovery reads the buffer with
+ * same-value atomics and never changes its contents, but no other work may
+ * write that memory while it runs.  d_base == NULL creates a context without
+ * a map: reductions then run side-agnostic.
+ * Replaces: the harness' `-i` init launch on (A, B) -- QuickRunCUDA.cpp:477-487
+ * calling tests/side_aware.cu:72 `init`. */
+int qrc_ctx_create(qrc_ctx** out, int device, const void* d_base, size_t bytes, void* stream);
+
+/* Free a context and its device scratch.  NULL is accepted. */
+int qrc_ctx_destroy(qrc_ctx* ctx);
+
+/* Copy the discovery result.  Replaces the init kernel's debug printout
+ * (tests/side_aware.cu:95-197). */
+int qrc_ctx_get_info(const qrc_ctx* ctx, qrc_side_info* info);
+
+/* Select the read mode (qrc_mode) for later reductions on this context.
+ * Replaces the compile-time FORCE_RANDOM_SIDE / FORCE_WRONG_SIDE defines
+ * (tests/side_aware.cu:19-20). */
+int qrc_ctx_set_mode(qrc_ctx* ctx, int mode);
+
+/* Launch shape for later reductions: blocks per SM (1 or 2) and threads per
+ * block (256, 512 or 1024; blocks_per_sm * threads <= 2048).  Default 1 x 1024,
+ * the reference's `-p -t 1024` (QuickRunCUDA.cpp:365-369). */
+int qrc_ctx_set_launch(qrc_ctx* ctx, int blocks_per_sm, int threads_per_block);
+
+/* *d_out = max_i |d_in[i]| over n floats (IEEE maxNum: NaN inputs are ignored,
+ * -0 gives +0, n == 0 gives +0).  d_in must be 4-byte aligned; the side-aware
+ * path applies when [d_in, d_in + n) lies inside the context's buffer.
+ * Bit-exact and deterministic.  Asynchronous on `stream`.
+ * Replaces: one timed launch of `kernel` (QuickRunCUDA.cpp:528-532 ->
+ * tests/side_aware.cu:257-395) with C[0] as the output. */
+int qrc_absmax_f32(const float* d_in, size_t n, float* d_out, qrc_ctx* ctx, void* stream);
+
+/* Same result from a host buffer: copies h_in to a device staging buffer owned
+ * by the context (allocated and side-mapped on first use, regrown when n grows),
+ * reduces it and copies the result to *h_out.  Synchronous.  Pinned host memory
+ * gives full PCIe bandwidth.
+ * Replaces: the harness' fill-and-copy of A (QuickRunCUDA.cpp:432-457) followed
+ * by a kernel launch and the C dump (:594-615). */
+int qrc_absmax_f32_host(const float* h_in, size_t n, float* h_out, qrc_ctx* ctx, void* stream);
+
+/* Fused per-tensor FP8 quantize of n bf16 values (raw bit patterns):
+ *   amax = max |x| (maxNum), *d_scale = 448 / amax (IEEE division; 1 when amax
+ *   is 0 or infinite), d_q[i] = e4m3(x[i] * scale) with round-to-nearest-even
+ *   and saturation to +-448 (OCP OFP8 E4M3).  d_amax (may be NULL) receives
+ *   amax.  Asynchronous.  No reference counterpart: the quantize extends the
+ *   reduction of tests/side_aware.cu:216-219 to the quant_infer use case. */
+int qrc_amax_quant_e4m3(const uint16_t* d_in_bf16, size_t n, uint8_t* d_q, float* d_scale,
+                        float* d_amax, qrc_ctx* ctx, void* stream);
+
+/* Synthetic inputs generated on the device; element i of the stream is a pure
+ * function of (seed, offset + i), so shards of one stream can be generated
+ * independently.  uniform[-1,1) on a 2^-23 grid; normal(0, sigma) is the
+ * Irwin-Hall sum of twelve 24-bit uniforms (sigma a power of two keeps it
+ * bit-reproducible).  The host variants produce identical bits.
+ * No reference counterpart: the harness fills A with masked mt19937_64 bits or
+ * zeros only (QuickRunCUDA.cpp:432-463). */
+int qrc_fill_uniform_f32(float* d_out, size_t n, uint64_t seed, uint64_t offset, void* stream);
+int qrc_fill_normal_f32(float* d_out, size_t n, uint64_t seed, uint64_t offset, float sigma, void* stream);
+int qrc_fill_normal_bf16(uint16_t* d_out, size_t n, uint64_t seed, uint64_t offset, float sigma, void* stream);
+int qrc_host_fill_uniform_f32(float* h_out, size_t n, uint64_t seed, uint64_t offset);
+int qrc_host_fill_normal_f32(float* h_out, size_t n, uint64_t seed, uint64_t offset, float sigma);
+
+/* Seeded outlier placement used by the synthetic workloads: index in [0, n)
+ * and sign (+1 / -1). */
+uint64_t qrc_outlier_index(uint64_t seed, uint64_t n);
+int qrc_outlier_sign(uint64_t seed);
+
+/* Human-readable names. */
+const char* qrc_status_string(int status);
+const char* qrc_side_status_string(uint32_t side_status);
+
+/* Last CUDA runtime error code seen by the library on this thread (0 = none). */
+int qrc_last_cuda_error(void);
+
+/* Library version (major * 10000 + minor * 100 + patch). */
+int qrc_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QRC_B200_H */

@@ -1,0 +1,442 @@
+// qrc_abi.cu -- libqrc_b200.so: the C ABI declared in include/qrc_b200.h.
+//
+// The device code is the plugin kernel file itself (side_aware_b200.cu, with
+// its `init`/`kernel` wrappers compiled out); this file adds kernels with
+// launch shapes chosen by the library, the FP8 quantize pass, the synthetic
+// generators and the host-side context that owns the side map.
+#define QRC_NO_PLUGIN_ABI
+#include "side_aware_b200.cu"
+#include "qrc_gen.cuh"
+#include "../../include/qrc_b200.h"
+#include "../../include/qrc_b200_debug.h"
+
+#include <cuda_runtime.h>
+#include <cstring>
+#include <cstdlib>
+#include <omp.h>
+
+#define QRC_API extern "C" __attribute__((visibility("default")))
+
+// ---------------------------------------------------------------------------
+// Kernels
+// ---------------------------------------------------------------------------
+
+__global__ void __launch_bounds__(1024, 1)
+qrc_k_discover(const void* base, qrc_u64 bytes, qrc_u32* map) {
+    qrc::discover(base, bytes, map);
+}
+
+// 64 registers per thread at every shape: 1024 x 1, 512 x 2, 256 x 4 per SM.
+template <int T>
+__global__ void __launch_bounds__(T, 1024 / T)
+qrc_k_absmax_f32(const float* in, qrc_u64 n, qrc_u32* map, float* out, qrc_u32 mode) {
+    qrc::reduce_run<qrc::OpAbsF32>(in, n, map, out, nullptr, mode);
+}
+
+template <int T>
+__global__ void __launch_bounds__(T, 1024 / T)
+qrc_k_amax_bf16(const uint16_t* in, qrc_u64 n, qrc_u32* map, float* amax, float* scale, qrc_u32 mode) {
+    qrc::reduce_run<qrc::OpAbsBF16>(in, n, map, amax, scale, mode);
+}
+
+__global__ void qrc_k_set_word(qrc_u32* map, qrc_u32 idx, qrc_u32 val) { map[idx] = val; }
+
+// e4m3x2 pack: upper byte from `hi`, lower byte from `lo`; RNE, saturating.
+static __device__ __forceinline__ unsigned short cvt_e4m3x2(float hi, float lo) {
+    unsigned short r;
+    asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+    return r;
+}
+
+// Two bf16 (one 32-bit word, element 0 in the low half) -> two e4m3 bytes.
+static __device__ __forceinline__ unsigned short quant_word(qrc_u32 w, float s) {
+    const float f0 = __uint_as_float(w << 16), f1 = __uint_as_float(w & 0xFFFF0000u);
+    return cvt_e4m3x2(__fmul_rn(f1, s), __fmul_rn(f0, s));
+}
+
+// Quantize pass: 8 bf16 (16 B) in -> 8 e4m3 (8 B) out per unit, four units in
+// flight per thread.  Vector path needs in % 16 == 0 and q % 8 == 0; any other
+// alignment takes the element path.
+__global__ void __launch_bounds__(512, 2)
+qrc_k_quant_e4m3(const uint16_t* in, qrc_u64 n, uint8_t* q, const float* scale_p) {
+    const float s = *scale_p;
+    const qrc_u64 tid = (qrc_u64)blockIdx.x * blockDim.x + threadIdx.x;
+    const qrc_u64 stride = (qrc_u64)gridDim.x * blockDim.x;
+    const bool vec = (((qrc_u64)in & 15) == 0) && (((qrc_u64)q & 7) == 0);
+    const qrc_u64 nv = vec ? n / 8 : 0;
+    for (qrc_u64 i = tid; i < nv; i += 4 * stride) {
+        uint4 v[4];
+        #pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const qrc_u64 j = i + u * stride;
+            if (j < nv) v[u] = qrc::ld_stream16((qrc_u64)(in + 8 * j));
+        }
+        #pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const qrc_u64 j = i + u * stride;
+            if (j < nv) {
+                uint2 o;
+                o.x = (qrc_u32)quant_word(v[u].x, s) | ((qrc_u32)quant_word(v[u].y, s) << 16);
+                o.y = (qrc_u32)quant_word(v[u].z, s) | ((qrc_u32)quant_word(v[u].w, s) << 16);
+                __stcs((uint2*)(q + 8 * j), o);
+            }
+        }
+    }
+    for (qrc_u64 e = nv * 8 + tid; e < n; e += stride) {
+        const float f = __uint_as_float((qrc_u32)in[e] << 16);
+        q[e] = (uint8_t)(cvt_e4m3x2(0.0f, __fmul_rn(f, s)) & 0xFFu);
+    }
+}
+
+__global__ void qrc_k_debug_cvt_e4m3(const float* in, qrc_u64 n, uint8_t* out) {
+    for (qrc_u64 i = (qrc_u64)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (qrc_u64)gridDim.x * blockDim.x)
+        out[i] = (uint8_t)(cvt_e4m3x2(0.0f, in[i]) & 0xFFu);
+}
+
+__global__ void qrc_k_fill_uniform(float* out, qrc_u64 n, qrc_u64 key, qrc_u64 offset) {
+    for (qrc_u64 i = (qrc_u64)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (qrc_u64)gridDim.x * blockDim.x)
+        out[i] = qrc_gen::uniform_pm1(key, offset + i);
+}
+__global__ void qrc_k_fill_normal(float* out, qrc_u64 n, qrc_u64 key, qrc_u64 offset, float sigma) {
+    for (qrc_u64 i = (qrc_u64)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (qrc_u64)gridDim.x * blockDim.x)
+        out[i] = qrc_gen::normal01(key, offset + i) * sigma;
+}
+__global__ void qrc_k_fill_normal_bf16(uint16_t* out, qrc_u64 n, qrc_u64 key, qrc_u64 offset, float sigma) {
+    for (qrc_u64 i = (qrc_u64)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (qrc_u64)gridDim.x * blockDim.x)
+        out[i] = qrc_gen::f32_to_bf16_rn(__fmul_rn(qrc_gen::normal01(key, offset + i), sigma));
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+
+namespace {
+
+thread_local int g_last_cuda = 0;
+
+#define QRC_CK(call)                                                      \
+    do {                                                                  \
+        cudaError_t e_ = (call);                                          \
+        if (e_ != cudaSuccess) { g_last_cuda = (int)e_; return QRC_ERR_CUDA; } \
+    } while (0)
+
+// Makes `dev` current for the scope and restores the caller's device.
+struct DeviceScope {
+    int prev = -1, ok = 0;
+    explicit DeviceScope(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) { prev = -1; }
+        ok = (prev == dev) || (cudaSetDevice(dev) == cudaSuccess);
+    }
+    ~DeviceScope() { if (prev >= 0) cudaSetDevice(prev); }
+};
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+constexpr size_t kMapHeaderWords = qrc::O_PAGE_BITS;
+
+}  // namespace
+
+struct qrc_ctx {
+    int device = 0;
+    int num_sms = 0;
+    int mode = QRC_MODE_SIDE_AWARE;
+    int blocks_per_sm = 1;
+    int threads = 1024;
+    const void* base = nullptr;
+    size_t bytes = 0;
+    qrc_u32* d_map = nullptr;
+    size_t map_words = 0;
+    qrc_side_info info{};
+    float* d_scalars = nullptr;     // [0] amax scratch, [1] host-path result
+    float* d_stage = nullptr;       // host-buffer staging (qrc_absmax_f32_host)
+    size_t stage_cap = 0;           // floats
+    qrc_ctx* stage_ctx = nullptr;   // side map of the staging buffer
+};
+
+static void fill_info(qrc_ctx* c, const qrc_u32* h) {
+    qrc_side_info& i = c->info;
+    i.status = h[qrc::H_STATUS];
+    i.mask = h[qrc::H_MASK];
+    i.mask_measured = h[qrc::H_MASK_MEASURED];
+    i.chunk_bytes = 1u << (h[qrc::H_CHUNK_LOG2] & 31u);
+    i.num_sms_measured = h[qrc::H_NSM];
+    i.sms_side0 = h[qrc::H_NSIDE0];
+    i.sms_side1 = h[qrc::H_NSIDE1];
+    i.num_pages = h[qrc::H_NPAGES];
+    i.verify_probes = h[qrc::H_VERIFY_N];
+    i.verify_mismatches = h[qrc::H_VERIFY_BAD];
+    i.cal_lat_side0 = h[qrc::H_LAT0];
+    i.cal_lat_side1 = h[qrc::H_LAT1];
+    i.sm_lat_cluster0 = h[qrc::H_SM_C0];
+    i.sm_lat_cluster1 = h[qrc::H_SM_C1];
+    i.discover_smid = h[qrc::H_SMID_LAST];
+}
+
+static int launch_absmax(qrc_ctx* c, const float* in, size_t n, float* out, cudaStream_t s) {
+    const int grid = c->num_sms * c->blocks_per_sm;
+    const qrc_u32 mode = (qrc_u32)c->mode;
+    switch (c->threads) {
+        case 1024: qrc_k_absmax_f32<1024><<<grid, 1024, 0, s>>>(in, n, c->d_map, out, mode); break;
+        case 512:  qrc_k_absmax_f32<512><<<grid, 512, 0, s>>>(in, n, c->d_map, out, mode); break;
+        default:   qrc_k_absmax_f32<256><<<grid, 256, 0, s>>>(in, n, c->d_map, out, mode); break;
+    }
+    QRC_CK(cudaGetLastError());
+    return QRC_OK;
+}
+
+QRC_API int qrc_ctx_create(qrc_ctx** out, int device, const void* d_base, size_t bytes, void* stream) {
+    if (!out) return QRC_ERR_INVALID;
+    *out = nullptr;
+    if (d_base && ((uintptr_t)d_base & 3)) return QRC_ERR_INVALID;
+    int ndev = 0;
+    QRC_CK(cudaGetDeviceCount(&ndev));
+    if (device < 0 || device >= ndev) return QRC_ERR_DEVICE;
+    DeviceScope scope(device);
+    if (!scope.ok) return QRC_ERR_DEVICE;
+    int major = 0, sms = 0;
+    QRC_CK(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device));
+    QRC_CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
+    if (major != 10) return QRC_ERR_DEVICE;
+
+    qrc_ctx* c = new qrc_ctx();
+    c->device = device;
+    c->num_sms = sms;
+    c->base = d_base;
+    c->bytes = d_base ? bytes : 0;
+    const uint64_t pages = d_base ? (((uintptr_t)d_base + bytes + qrc::kPage - 1) / qrc::kPage -
+                                     (uintptr_t)d_base / qrc::kPage) : 0;
+    size_t cap_words = (size_t)((pages + 31) / 32) + 1;
+    if (cap_words < qrc::kDefaultPageWords) cap_words = qrc::kDefaultPageWords;
+    c->map_words = kMapHeaderWords + cap_words;
+    cudaStream_t s = as_stream(stream);
+    int rc = QRC_OK;
+    do {
+        if (cudaMalloc(&c->d_map, c->map_words * 4) != cudaSuccess ||
+            cudaMalloc(&c->d_scalars, 64) != cudaSuccess) { rc = QRC_ERR_CUDA; break; }
+        if (cudaMemsetAsync(c->d_map, 0, c->map_words * 4, s) != cudaSuccess ||
+            cudaMemsetAsync(c->d_scalars, 0, 64, s) != cudaSuccess) { rc = QRC_ERR_CUDA; break; }
+        qrc_k_set_word<<<1, 1, 0, s>>>(c->d_map, qrc::H_PAGE_WORDS_CAP, (qrc_u32)cap_words);
+        if (d_base) qrc_k_discover<<<sms, 1024, 0, s>>>(d_base, (qrc_u64)bytes, c->d_map);
+        if (cudaGetLastError() != cudaSuccess || cudaStreamSynchronize(s) != cudaSuccess) { rc = QRC_ERR_CUDA; break; }
+        qrc_u32 h[256];
+        if (cudaMemcpy(h, c->d_map, sizeof(h), cudaMemcpyDeviceToHost) != cudaSuccess) { rc = QRC_ERR_CUDA; break; }
+        fill_info(c, h);
+        if (!d_base) c->info.status = QRC_SIDE_NOT_RUN;
+    } while (0);
+    if (rc != QRC_OK) {
+        g_last_cuda = (int)cudaGetLastError();
+        if (c->d_map) cudaFree(c->d_map);
+        if (c->d_scalars) cudaFree(c->d_scalars);
+        delete c;
+        return rc;
+    }
+    *out = c;
+    return QRC_OK;
+}
+
+QRC_API int qrc_ctx_destroy(qrc_ctx* c) {
+    if (!c) return QRC_OK;
+    DeviceScope scope(c->device);
+    if (c->stage_ctx) qrc_ctx_destroy(c->stage_ctx);
+    if (c->d_stage) cudaFree(c->d_stage);
+    if (c->d_map) cudaFree(c->d_map);
+    if (c->d_scalars) cudaFree(c->d_scalars);
+    delete c;
+    return QRC_OK;
+}
+
+QRC_API int qrc_ctx_get_info(const qrc_ctx* c, qrc_side_info* info) {
+    if (!c || !info) return QRC_ERR_INVALID;
+    *info = c->info;
+    return QRC_OK;
+}
+
+QRC_API int qrc_ctx_set_mode(qrc_ctx* c, int mode) {
+    if (!c || mode < QRC_MODE_SIDE_AWARE || mode > QRC_MODE_STREAM) return QRC_ERR_INVALID;
+    c->mode = mode;
+    if (c->stage_ctx) c->stage_ctx->mode = mode;
+    return QRC_OK;
+}
+
+QRC_API int qrc_ctx_set_launch(qrc_ctx* c, int blocks_per_sm, int threads) {
+    if (!c || (threads != 256 && threads != 512 && threads != 1024)) return QRC_ERR_INVALID;
+    if (blocks_per_sm < 1 || blocks_per_sm * threads > 2048) return QRC_ERR_INVALID;
+    c->blocks_per_sm = blocks_per_sm;
+    c->threads = threads;
+    if (c->stage_ctx) qrc_ctx_set_launch(c->stage_ctx, blocks_per_sm, threads);
+    return QRC_OK;
+}
+
+QRC_API int qrc_absmax_f32(const float* d_in, size_t n, float* d_out, qrc_ctx* c, void* stream) {
+    if (!c || !d_out || (n && !d_in) || ((uintptr_t)d_in & 3)) return QRC_ERR_INVALID;
+    if (n > ((size_t)1 << 61)) return QRC_ERR_RANGE;
+    DeviceScope scope(c->device);
+    if (!scope.ok) return QRC_ERR_STATE;
+    return launch_absmax(c, d_in, n, d_out, as_stream(stream));
+}
+
+QRC_API int qrc_absmax_f32_host(const float* h_in, size_t n, float* h_out, qrc_ctx* c, void* stream) {
+    if (!c || !h_out || (n && !h_in)) return QRC_ERR_INVALID;
+    DeviceScope scope(c->device);
+    if (!scope.ok) return QRC_ERR_STATE;
+    cudaStream_t s = as_stream(stream);
+    if (n > c->stage_cap) {
+        if (c->stage_ctx) { qrc_ctx_destroy(c->stage_ctx); c->stage_ctx = nullptr; }
+        if (c->d_stage) { cudaFree(c->d_stage); c->d_stage = nullptr; c->stage_cap = 0; }
+        QRC_CK(cudaMalloc(&c->d_stage, n * sizeof(float)));
+        c->stage_cap = n;
+        const int rc = qrc_ctx_create(&c->stage_ctx, c->device, c->d_stage, n * sizeof(float), stream);
+        if (rc != QRC_OK) return rc;
+        c->stage_ctx->mode = c->mode;
+        c->stage_ctx->blocks_per_sm = c->blocks_per_sm;
+        c->stage_ctx->threads = c->threads;
+    }
+    qrc_ctx* sc = c->stage_ctx ? c->stage_ctx : c;
+    if (n) QRC_CK(cudaMemcpyAsync(c->d_stage, h_in, n * sizeof(float), cudaMemcpyHostToDevice, s));
+    const int rc = launch_absmax(sc, c->d_stage, n, c->d_scalars + 1, s);
+    if (rc != QRC_OK) return rc;
+    QRC_CK(cudaMemcpyAsync(h_out, c->d_scalars + 1, sizeof(float), cudaMemcpyDeviceToHost, s));
+    QRC_CK(cudaStreamSynchronize(s));
+    return QRC_OK;
+}
+
+QRC_API int qrc_amax_quant_e4m3(const uint16_t* d_in, size_t n, uint8_t* d_q, float* d_scale,
+                                float* d_amax, qrc_ctx* c, void* stream) {
+    if (!c || !d_scale || (n && (!d_in || !d_q)) || ((uintptr_t)d_in & 1)) return QRC_ERR_INVALID;
+    DeviceScope scope(c->device);
+    if (!scope.ok) return QRC_ERR_STATE;
+    cudaStream_t s = as_stream(stream);
+    float* amax = d_amax ? d_amax : c->d_scalars;
+    const int grid = c->num_sms * c->blocks_per_sm;
+    switch (c->threads) {
+        case 1024: qrc_k_amax_bf16<1024><<<grid, 1024, 0, s>>>(d_in, n, c->d_map, amax, d_scale, c->mode); break;
+        case 512:  qrc_k_amax_bf16<512><<<grid, 512, 0, s>>>(d_in, n, c->d_map, amax, d_scale, c->mode); break;
+        default:   qrc_k_amax_bf16<256><<<grid, 256, 0, s>>>(d_in, n, c->d_map, amax, d_scale, c->mode); break;
+    }
+    QRC_CK(cudaGetLastError());
+    if (n) {
+        qrc_k_quant_e4m3<<<c->num_sms * 2, 512, 0, s>>>(d_in, n, d_q, d_scale);
+        QRC_CK(cudaGetLastError());
+    }
+    return QRC_OK;
+}
+
+// ---- generators ------------------------------------------------------------
+
+static int fill_grid(void) {
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    return sms * 8;
+}
+
+QRC_API int qrc_fill_uniform_f32(float* d_out, size_t n, uint64_t seed, uint64_t offset, void* stream) {
+    if (n && !d_out) return QRC_ERR_INVALID;
+    if (!n) return QRC_OK;
+    qrc_k_fill_uniform<<<fill_grid(), 256, 0, as_stream(stream)>>>(d_out, n, qrc_gen::key_of(seed), offset);
+    QRC_CK(cudaGetLastError());
+    return QRC_OK;
+}
+
+QRC_API int qrc_fill_normal_f32(float* d_out, size_t n, uint64_t seed, uint64_t offset, float sigma, void* stream) {
+    if (n && !d_out) return QRC_ERR_INVALID;
+    if (!n) return QRC_OK;
+    qrc_k_fill_normal<<<fill_grid(), 256, 0, as_stream(stream)>>>(d_out, n, qrc_gen::key_of(seed), offset, sigma);
+    QRC_CK(cudaGetLastError());
+    return QRC_OK;
+}
+
+QRC_API int qrc_fill_normal_bf16(uint16_t* d_out, size_t n, uint64_t seed, uint64_t offset, float sigma, void* stream) {
+    if (n && !d_out) return QRC_ERR_INVALID;
+    if (!n) return QRC_OK;
+    qrc_k_fill_normal_bf16<<<fill_grid(), 256, 0, as_stream(stream)>>>(d_out, n, qrc_gen::key_of(seed), offset, sigma);
+    QRC_CK(cudaGetLastError());
+    return QRC_OK;
+}
+
+QRC_API int qrc_host_fill_uniform_f32(float* h_out, size_t n, uint64_t seed, uint64_t offset) {
+    if (n && !h_out) return QRC_ERR_INVALID;
+    const uint64_t key = qrc_gen::key_of(seed);
+    #pragma omp parallel for schedule(static)
+    for (size_t i = 0; i < n; i++) h_out[i] = qrc_gen::uniform_pm1(key, offset + i);
+    return QRC_OK;
+}
+
+QRC_API int qrc_host_fill_normal_f32(float* h_out, size_t n, uint64_t seed, uint64_t offset, float sigma) {
+    if (n && !h_out) return QRC_ERR_INVALID;
+    const uint64_t key = qrc_gen::key_of(seed);
+    #pragma omp parallel for schedule(static)
+    for (size_t i = 0; i < n; i++) h_out[i] = qrc_gen::normal01(key, offset + i) * sigma;
+    return QRC_OK;
+}
+
+QRC_API uint64_t qrc_outlier_index(uint64_t seed, uint64_t n) { return qrc_gen::outlier_index(seed, n); }
+QRC_API int qrc_outlier_sign(uint64_t seed) { return qrc_gen::outlier_sign(seed); }
+
+// ---- strings, version, diagnostics -------------------------------------------
+
+QRC_API const char* qrc_status_string(int st) {
+    switch (st) {
+        case QRC_OK: return "ok";
+        case QRC_ERR_INVALID: return "invalid argument";
+        case QRC_ERR_CUDA: return "CUDA runtime error";
+        case QRC_ERR_DEVICE: return "no such sm_100 device";
+        case QRC_ERR_RANGE: return "input too large";
+        case QRC_ERR_STATE: return "context used on another device";
+        default: return "unknown status";
+    }
+}
+
+QRC_API const char* qrc_side_status_string(uint32_t st) {
+    switch (st) {
+        case QRC_SIDE_OK: return "side-aware";
+        case QRC_SIDE_TOO_SMALL: return "buffer holds no full 2 MiB page";
+        case QRC_SIDE_NO_SM_SPLIT: return "SM latencies did not split into two sides";
+        case QRC_SIDE_NO_HASH: return "no in-page address bit changed the side";
+        case QRC_SIDE_BAD_HASH: return "hash granule below 512 bytes";
+        case QRC_SIDE_NO_CAL_SPLIT: return "calibration words not separable";
+        case QRC_SIDE_VERIFY_FAILED: return "side map failed verification";
+        case QRC_SIDE_TOO_MANY_PAGES: return "too many pages for the map";
+        case QRC_SIDE_UNALIGNED: return "buffer not 4-byte aligned";
+        case QRC_SIDE_NOT_RUN: return "no buffer given: side-agnostic";
+        default: return "unknown side status";
+    }
+}
+
+QRC_API int qrc_last_cuda_error(void) { return g_last_cuda; }
+QRC_API int qrc_version(void) { return 10000; }
+
+QRC_API int qrc_ctx_read_map(const qrc_ctx* c, uint32_t* h, size_t words, size_t* total) {
+    if (!c || (words && !h)) return QRC_ERR_INVALID;
+    if (total) *total = c->map_words;
+    if (words > c->map_words) words = c->map_words;
+    DeviceScope scope(c->device);
+    QRC_CK(cudaDeviceSynchronize());
+    if (words) QRC_CK(cudaMemcpy(h, c->d_map, words * 4, cudaMemcpyDeviceToHost));
+    return QRC_OK;
+}
+
+QRC_API int qrc_ctx_clear_diagnostics(qrc_ctx* c) {
+    if (!c) return QRC_ERR_INVALID;
+    DeviceScope scope(c->device);
+    QRC_CK(cudaDeviceSynchronize());
+    QRC_CK(cudaMemset(c->d_map + qrc::H_ERR, 0, 8 * 4));
+    return QRC_OK;
+}
+
+QRC_API int qrc_is_checked_build(void) {
+#ifdef QRC_CHECKED
+    return 1;
+#else
+    return 0;
+#endif
+}
+
+QRC_API int qrc_debug_cvt_e4m3(const float* d_in, size_t n, uint8_t* d_out, void* stream) {
+    if (n && (!d_in || !d_out)) return QRC_ERR_INVALID;
+    if (!n) return QRC_OK;
+    qrc_k_debug_cvt_e4m3<<<fill_grid(), 256, 0, as_stream(stream)>>>(d_in, n, d_out);
+    QRC_CK(cudaGetLastError());
+    return QRC_OK;
+}
+
+QRC_API void* qrc_ctx_map_device_ptr(const qrc_ctx* c) { return c ? (void*)c->d_map : nullptr; }

@@ -1,0 +1,663 @@
+// side_aware_b200.cu -- L2-side-aware FP32 absmax for B200 (sm_100a).
+//
+// A drop-in kernel file for the QuickRunCUDA harness: it exports the harness'
+// plugin ABI (`init` + `kernel`, QuickRunCUDA.cpp:408-411 and :466-499), so
+//
+//   QuickRunCUDA -i -p -t 1024 -A 1000000000 -0 1000000000 -T 100 -P 4.0 -U GB/s side_aware_b200.cu
+//
+// runs it exactly like the reference's tests/side_aware.cu.  The file is
+// self-contained (no includes) so that NVRTC can compile it with the harness'
+// options; the C-ABI library (qrc_abi.cu) includes it with QRC_NO_PLUGIN_ABI
+// defined and launches the same device code from its own entry points.
+//
+// Plugin arguments (same slots as the reference, side_aware.cu:72 and :257):
+//   A        input floats (the harness allocates it with cuMemAlloc, so it is
+//            2 MiB aligned; any 4-byte aligned pointer works here)
+//   B        side map / scratch, zeroed by the harness before init
+//            (QuickRunCUDA.cpp:461-463); layout below, about 20 KiB
+//   C        C[0] receives absmax(A) after every `kernel` launch
+//   arg0     number of floats (`-0`)
+//   arg1     read mode (`-1`): 0 side-aware, 1 page bits ignored (the
+//            reference's FORCE_RANDOM_SIDE ablation), 2 every chunk read from
+//            the far side (FORCE_WRONG_SIDE), 3 side-agnostic grid-stride stream.
+//            `-H '#define FORCE_RANDOM_SIDE'` / FORCE_WRONG_SIDE also work.
+//
+// How B200 is modelled (the reference's model, side_aware.cu:8-12, re-measured
+// here by discovery rather than assumed):
+//   * each physical address is homed in the L2 of one of the two dies ("sides");
+//   * inside a 2 MiB page the side is parity(addr & mask) XOR a per-page bit,
+//     where mask covers address bits 4..20 and its lowest set bit is the chunk
+//     size C (4 KiB on GB200: mask 0x1EF000, side_aware.cu:49);
+//   * so the two C-byte halves of every 2C-aligned "pair" sit on opposite sides.
+//
+// Discovery (`init`, once per allocation) -- replaces side_aware.cu:72-210:
+//   phase 1  every CTA times a dependent chain of same-value atomicCAS on a
+//            word of the first full 2 MiB page ("anchor"); the chain never
+//            changes memory (CAS writes back the value it read), unlike the
+//            reference's exchange-then-restore (side_aware.cu:58-65).
+//   phase 2  the last CTA to arrive (atomic ticket after a fence):
+//            - splits SMs into two latency clusters (1-D 2-means, not the mean
+//              threshold of side_aware.cu:94-100); side 0 = near the anchor,
+//              so labels are absolute rather than relative to whichever SM
+//              finished last (fixes the unlabelled page bits of :176-180);
+//            - probes anchor ^ (1<<b), b = 4..20, from 21 warps at once to find
+//              the mask (side_aware.cu:125-157 did this serially);
+//            - calibrates this SM's latency to a known side-0 and side-1 word,
+//              then probes one word per 2 MiB page from 30 warps in parallel
+//              (side_aware.cu:173-190 probed ~1,900 pages serially);
+//            - verifies the model on 80 extra probes; if it mispredicts more
+//              than 1 in 8 the map is marked unusable and the reduction runs
+//              side-agnostic (still exact).
+//   Every wait in discovery is a bounded dependent chain; nothing spins.
+//
+// Reduction (`kernel`) -- replaces side_aware.cu:257-395:
+//   * any grid and any block size that is a multiple of 32 (the reference
+//     needed exactly one 1024-thread block per SM, :266-269);
+//   * each CTA reads its SM's side from the map and its warps pull 8-pair
+//     "grabs" from that side's atomic work queue (one counter per side); for
+//     every pair a warp reads the C-byte half homed on its own side.  Both
+//     queues walk every pair, one half each, so every byte is read exactly once
+//     whatever the map says -- the map only decides locality, never coverage;
+//   * per element max(acc, |x|) with IEEE maxNum semantics written in PTX
+//     (NaN never wins, -0 -> +0, denormals kept even under -use_fast_math);
+//   * warp max with redux.sync.max.u32 on the (non-negative) float bits, one
+//     smem step per block, one atomicMax per block, then a fenced ticket: the
+//     last CTA moves the result to C[0] and resets accumulator and queues, so
+//     back-to-back launches need no host work (fixes the unfenced
+//     scratch-then-ticket order of side_aware.cu:371-374).
+
+#ifndef QRC_SIDE_AWARE_B200_CU
+#define QRC_SIDE_AWARE_B200_CU
+
+typedef unsigned int qrc_u32;
+typedef unsigned long long qrc_u64;
+
+#define QRC_DEV static __device__ __forceinline__
+
+namespace qrc {
+
+constexpr qrc_u32 kMagic = 0x51525341u;         // 'QRSA'
+constexpr qrc_u64 kPage = 2ull * 1024 * 1024;   // side bit granularity (2 MiB pages)
+constexpr int kProbeIters = 32;                  // dependent atomics per latency probe
+constexpr int kMaxSm = 256;
+constexpr qrc_u32 kPairsPerGrab = 8;             // pairs a warp takes per queue atomic
+constexpr int kVerifyRandom = 64;
+constexpr int kVerifyCal = 8;                    // anchor + partner re-probes in verification
+constexpr int kCalProbes = 16;                   // per side, calibration wave
+constexpr int kDiagPages = 2048;                 // raw page latencies kept for diagnostics
+constexpr qrc_u32 kDefaultPageWords = 1024;      // page-bit capacity (32768 pages = 64 GiB)
+
+// Side map layout (32-bit words).  The buffer must start zeroed.
+enum : qrc_u32 {
+    H_MAGIC = 0, H_STATUS = 1, H_MASK = 2, H_CHUNK_LOG2 = 3, H_NSM = 4, H_NSIDE0 = 5,
+    H_NSIDE1 = 6, H_NPAGES = 7, H_BASE_LO = 8, H_BASE_HI = 9, H_BYTES_LO = 10, H_BYTES_HI = 11,
+    H_VERIFY_N = 12, H_VERIFY_BAD = 13, H_LAT0 = 14, H_LAT1 = 15, H_INIT_TICKET = 16,
+    H_RUN_TICKET = 17, H_ACC = 18, H_PAGE_WORDS_CAP = 19, H_MASK_MEASURED = 20,
+    H_SM_C0 = 21, H_SM_C1 = 22, H_BIT_C0 = 23, H_BIT_C1 = 24, H_SMID_LAST = 25,
+    H_QUEUE0 = 32, H_QUEUE1 = 64,                  // each on its own 128-byte line
+    H_ERR = 96, H_ERR_ADDR_LO = 97, H_ERR_ADDR_HI = 98,
+    H_COV_BYTES_LO = 100, H_COV_BYTES_HI = 101, H_COV_XOR_LO = 102, H_COV_XOR_HI = 103,
+    O_BITLAT = 128,                                // 21 raw latencies of the mask probes
+    O_SM_SIDE = 256,                               // per SM: 0 unknown, 1 side 0, 2 side 1
+    O_SM_LAT = 512,                                // per SM raw anchor latency (cycles)
+    O_PAGE_LAT = 1024,                             // first kDiagPages raw page latencies
+    O_PAGE_BITS = 4096,                            // one bit per 2 MiB page
+};
+
+enum : qrc_u32 {
+    ST_OK = 0, ST_TOO_SMALL = 1, ST_NO_SM_SPLIT = 2, ST_NO_HASH = 3, ST_BAD_HASH = 4,
+    ST_NO_CAL_SPLIT = 5, ST_VERIFY_FAILED = 6, ST_TOO_MANY_PAGES = 7, ST_UNALIGNED = 8,
+};
+
+enum : qrc_u32 { MODE_SIDE_AWARE = 0, MODE_IGNORE_PAGE_BITS = 1, MODE_WRONG_SIDE = 2, MODE_STREAM = 3 };
+
+QRC_DEV qrc_u32 smid() {
+    qrc_u32 r;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(r));
+    return r;
+}
+
+QRC_DEV int parity64(qrc_u64 x) { return __popcll(x) & 1; }
+
+// Cycles for kProbeIters dependent L2 atomics on `w`.  atomicCAS(w, v, v) with v
+// the current value writes back the value it found, so memory never changes,
+// and each CAS needs the previous result as its compare operand.  The first
+// CAS (untimed) brings the line into L2.  The clock reads take the chain's
+// value as an operand so they cannot move across it.
+QRC_DEV qrc_u32 probe_latency(qrc_u32* w) {
+    qrc_u32 v = atomicCAS(w, 0u, 0u);
+    qrc_u64 t0, t1;
+    asm volatile("mov.u64 %0, %%clock64;" : "=l"(t0) : "r"(v) : "memory");
+    #pragma unroll 1
+    for (int i = 0; i < kProbeIters; i++) v = atomicCAS(w, v, v);
+    asm volatile("mov.u64 %0, %%clock64;" : "=l"(t1) : "r"(v) : "memory");
+    return (qrc_u32)(t1 - t0);
+}
+
+// 1-D two-means on n values (n small, one thread).  Returns false when there
+// are fewer than two distinct values.  *lo/*hi are the cluster means.
+QRC_DEV bool two_means(const qrc_u32* v, int n, float* lo, float* hi) {
+    float mn = 3.4e38f, mx = 0.f;
+    int cnt = 0;
+    for (int i = 0; i < n; i++) {
+        if (v[i] == 0) continue;
+        mn = fminf(mn, (float)v[i]); mx = fmaxf(mx, (float)v[i]); cnt++;
+    }
+    if (cnt < 2 || !(mx > mn)) return false;
+    float c0 = mn, c1 = mx;
+    for (int it = 0; it < 32; it++) {
+        const float t = 0.5f * (c0 + c1);
+        float s0 = 0.f, s1 = 0.f; int n0 = 0, n1 = 0;
+        for (int i = 0; i < n; i++) {
+            if (v[i] == 0) continue;
+            const float x = (float)v[i];
+            if (x < t) { s0 += x; n0++; } else { s1 += x; n1++; }
+        }
+        if (n0 == 0 || n1 == 0) break;
+        c0 = s0 / n0; c1 = s1 / n1;
+    }
+    *lo = c0; *hi = c1;
+    return true;
+}
+
+// Separation required between near and far latency clusters (relative).
+QRC_DEV bool separated(float lo, float hi) { return hi > lo * 1.04f + 8.0f; }
+
+QRC_DEV qrc_u64 map_base(const qrc_u32* map) {
+    return ((qrc_u64)map[H_BASE_HI] << 32) | map[H_BASE_LO];
+}
+QRC_DEV qrc_u64 map_bytes(const qrc_u32* map) {
+    return ((qrc_u64)map[H_BYTES_HI] << 32) | map[H_BYTES_LO];
+}
+
+// ---------------------------------------------------------------------------
+// Discovery
+// ---------------------------------------------------------------------------
+
+// Probe address of page p: its first word inside [a, end).
+QRC_DEV qrc_u64 page_probe_addr(qrc_u64 a, qrc_u64 page_base, qrc_u64 p) {
+    qrc_u64 x = page_base + p * kPage;
+    if (x < a) x = (a + 3) & ~3ull;
+    return x;
+}
+
+QRC_DEV void write_header_and_publish(qrc_u32* map, qrc_u32 status, qrc_u64 a, qrc_u64 bytes) {
+    map[H_BASE_LO] = (qrc_u32)a; map[H_BASE_HI] = (qrc_u32)(a >> 32);
+    map[H_BYTES_LO] = (qrc_u32)bytes; map[H_BYTES_HI] = (qrc_u32)(bytes >> 32);
+    map[H_STATUS] = status;
+    __threadfence();
+    map[H_MAGIC] = kMagic;
+    __threadfence();
+}
+
+QRC_DEV void discover(const void* A, qrc_u64 bytes, qrc_u32* map) {
+    __shared__ int s_last;
+    __shared__ qrc_u32 s_lat[64];
+    __shared__ qrc_u32 s_cfg[8];   // 0 status, 1 mask, 2 lowbit, 3 thr, 4 near_is_0
+    __shared__ int s_bad;
+
+    // Probes are 4-byte atomics: only whole words inside [a, a + bytes) are touched.
+    const qrc_u64 a = (qrc_u64)A, end = a + (bytes & ~3ull);
+    const qrc_u64 anchor = (a + kPage - 1) & ~(kPage - 1);
+    const bool big_enough = ((a & 3) == 0) && bytes >= kPage && anchor + kPage <= end;
+
+    // ---- phase 1: every CTA times the anchor from its SM ----------------
+    if (threadIdx.x == 0) {
+        if (big_enough) {
+            const qrc_u32 sm = smid();
+            __nanosleep((sm & 7u) * 20000u);      // 8 waves, distinct words within a wave
+            qrc_u32* w = (qrc_u32*)(anchor + 4ull * ((sm >> 3) & 31u));
+            const qrc_u32 lat = probe_latency(w);
+            if (sm < (qrc_u32)kMaxSm) map[O_SM_LAT + sm] = lat;
+        }
+        __threadfence();
+        const qrc_u32 t = atomicInc(&map[H_INIT_TICKET], gridDim.x - 1);
+        s_last = (t == gridDim.x - 1);
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, W = blockDim.x >> 5;
+    const qrc_u64 page_base = a & ~(kPage - 1);
+    const qrc_u64 npages = (end - page_base + kPage - 1) / kPage;
+    qrc_u32 cap_words = map[H_PAGE_WORDS_CAP];
+    if (cap_words == 0) cap_words = kDefaultPageWords;
+
+    if (!big_enough || W < 2) {
+        if (threadIdx.x == 0) {
+            map[H_NPAGES] = (qrc_u32)npages;
+            write_header_and_publish(map, (a & 3) ? ST_UNALIGNED : ST_TOO_SMALL, a, bytes);
+        }
+        return;
+    }
+
+    // ---- SM classification (one thread) ----------------------------------
+    // Other CTAs' latencies are read through L2 (ld.cg): they were written by
+    // other SMs before their fenced ticket.
+    __shared__ qrc_u32 s_smlat[kMaxSm];
+    for (int i = threadIdx.x; i < kMaxSm; i += blockDim.x) s_smlat[i] = __ldcg(map + O_SM_LAT + i);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        qrc_u32 st = ST_OK;
+        float c0 = 0.f, c1 = 0.f;
+        if (!two_means(s_smlat, kMaxSm, &c0, &c1) || !separated(c0, c1)) st = ST_NO_SM_SPLIT;
+        const float thr = 0.5f * (c0 + c1);
+        qrc_u32 n0 = 0, n1 = 0, nsm = 0;
+        for (int i = 0; i < kMaxSm; i++) {
+            const qrc_u32 l = s_smlat[i];
+            if (l == 0) { map[O_SM_SIDE + i] = 0; continue; }
+            nsm++;
+            const qrc_u32 side = (st == ST_OK && (float)l >= thr) ? 1u : 0u;
+            map[O_SM_SIDE + i] = 1u + side;
+            if (side) n1++; else n0++;
+        }
+        map[H_NSM] = nsm; map[H_NSIDE0] = n0; map[H_NSIDE1] = n1;
+        map[H_SM_C0] = (qrc_u32)c0; map[H_SM_C1] = (qrc_u32)c1;
+        map[H_SMID_LAST] = smid();
+        s_cfg[0] = st;
+    }
+    __syncthreads();
+
+    // ---- mask discovery: 4 anchor probes + bits 4..20, one warp each ------
+    for (int it = warp; it < 21; it += W) {
+        if (lane == 0) {
+            const qrc_u64 x = it < 4 ? anchor : (anchor ^ (1ull << it));
+            s_lat[it] = probe_latency((qrc_u32*)x);
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < 21; i++) map[O_BITLAT + i] = s_lat[i];
+        qrc_u32 st = s_cfg[0], mask = 0, lowbit = 0;
+        float c0 = 0.f, c1 = 0.f;
+        if (st == ST_OK) {
+            if (!two_means(s_lat, 21, &c0, &c1) || !separated(c0, c1)) {
+                st = ST_NO_HASH;
+            } else {
+                const float thr = 0.5f * (c0 + c1);
+                const bool anchor_hi = (float)(s_lat[0] + s_lat[1] + s_lat[2] + s_lat[3]) * 0.25f >= thr;
+                bool anchors_agree = true;
+                for (int i = 0; i < 4; i++) anchors_agree &= (((float)s_lat[i] >= thr) == anchor_hi);
+                for (int b = 4; b <= 20; b++)
+                    if ((((float)s_lat[b] >= thr) != anchor_hi)) mask |= 1u << b;
+                if (!anchors_agree || mask == 0) st = ST_NO_HASH;
+                else {
+                    lowbit = __ffs(mask) - 1;
+                    if (lowbit < 9) st = ST_BAD_HASH;   // chunk must hold >= one 512 B warp row
+                }
+            }
+        }
+        map[H_MASK_MEASURED] = mask;
+        map[H_BIT_C0] = (qrc_u32)c0; map[H_BIT_C1] = (qrc_u32)c1;
+        s_cfg[0] = st; s_cfg[1] = mask; s_cfg[2] = lowbit;
+    }
+    __syncthreads();
+    qrc_u32 st = s_cfg[0];
+    const qrc_u32 mask = s_cfg[1];
+    const qrc_u64 partner = anchor ^ (1ull << s_cfg[2]);
+
+    // ---- calibration wave: side-0 anchor vs side-1 partner -----------------
+    if (st == ST_OK) {
+        for (int it = warp; it < 2 * kCalProbes; it += W)
+            if (lane == 0) s_lat[it] = probe_latency((qrc_u32*)((it & 1) ? partner : anchor));
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            float l0 = 0.f, l1 = 0.f;
+            for (int i = 0; i < 2 * kCalProbes; i++) {
+                if (i & 1) l1 += (float)s_lat[i]; else l0 += (float)s_lat[i];
+            }
+            l0 /= kCalProbes; l1 /= kCalProbes;
+            map[H_LAT0] = (qrc_u32)l0; map[H_LAT1] = (qrc_u32)l1;
+            if (!separated(fminf(l0, l1), fmaxf(l0, l1))) st = ST_NO_CAL_SPLIT;
+            const qrc_u64 nwords = (npages + 31) / 32;
+            if (nwords > cap_words) st = ST_TOO_MANY_PAGES;
+            s_cfg[0] = st;
+            s_cfg[3] = (qrc_u32)(0.5f * (l0 + l1));
+            s_cfg[4] = l0 < l1;
+        }
+        __syncthreads();
+        st = s_cfg[0];
+    }
+    const qrc_u32 thr = s_cfg[3];
+    const bool near_is_0 = s_cfg[4] != 0;
+    // side of an address from this SM's latency to it
+    #define QRC_CLASSIFY(lat) ((((lat) < thr) == near_is_0) ? 0 : 1)
+
+    // ---- page probes: warp k owns page-bit words k, k+W, ... --------------
+    if (st == ST_OK) {
+        const qrc_u64 nwords = (npages + 31) / 32;
+        for (qrc_u64 wd = warp; wd < nwords; wd += W) {
+            if (lane == 0) {
+                qrc_u32 word = 0;
+                for (int j = 0; j < 32; j++) {
+                    const qrc_u64 p = wd * 32 + j;
+                    if (p >= npages) break;
+                    const qrc_u64 x = page_probe_addr(a, page_base, p);
+                    const qrc_u32 lat = probe_latency((qrc_u32*)x);
+                    if (p < (qrc_u64)kDiagPages) map[O_PAGE_LAT + p] = lat;
+                    const qrc_u32 bit = (qrc_u32)QRC_CLASSIFY(lat) ^ (qrc_u32)parity64(x & mask);
+                    word |= bit << j;
+                }
+                map[O_PAGE_BITS + wd] = word;
+            }
+        }
+        if (threadIdx.x == 0) s_bad = 0;
+        __syncthreads();
+
+        // ---- verification: known anchors + pseudo-random words -----------
+        const int nver = 2 * kVerifyCal + kVerifyRandom;
+        for (int it = warp; it < nver; it += W) {
+            if (lane == 0) {
+                qrc_u64 x;
+                if (it < kVerifyCal) x = anchor;
+                else if (it < 2 * kVerifyCal) x = partner;
+                else {
+                    qrc_u64 h = (qrc_u64)(it + 1) * 0x9E3779B97F4A7C15ull;
+                    h ^= h >> 29; h *= 0xBF58476D1CE4E5B9ull; h ^= h >> 32;
+                    x = a + ((h % ((end - a) >> 2)) << 2);
+                }
+                const qrc_u64 p = (x - page_base) / kPage;
+                const int pbit = (map[O_PAGE_BITS + (p >> 5)] >> (p & 31)) & 1;
+                const int predicted = parity64(x & mask) ^ pbit;
+                const int measured = QRC_CLASSIFY(probe_latency((qrc_u32*)x));
+                if (predicted != measured) atomicAdd(&s_bad, 1);
+            }
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            map[H_VERIFY_N] = nver;
+            map[H_VERIFY_BAD] = (qrc_u32)s_bad;
+            if (s_bad * 8 > nver) st = ST_VERIFY_FAILED;
+            s_cfg[0] = st;
+        }
+        __syncthreads();
+        st = s_cfg[0];
+    }
+    #undef QRC_CLASSIFY
+
+    if (threadIdx.x == 0) {
+        map[H_MASK] = (st == ST_OK) ? mask : 0u;
+        map[H_CHUNK_LOG2] = (st == ST_OK) ? s_cfg[2] : 12u;
+        map[H_NPAGES] = (qrc_u32)npages;
+        write_header_and_publish(map, st, a, bytes);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Reduction
+// ---------------------------------------------------------------------------
+
+// acc = maxNum(acc, |x|): IEEE-754 maxNum (a NaN operand loses), no FTZ.
+QRC_DEV float absmax_step(float acc, float x) {
+    float r;
+    asm("{\n\t.reg .f32 t;\n\tabs.f32 t, %2;\n\tmax.f32 %0, %1, t;\n\t}" : "=f"(r) : "f"(acc), "f"(x));
+    return r;
+}
+
+// Same on two packed bf16 lanes (max.bf16x2 is maxNum as well).
+QRC_DEV qrc_u32 absmax_step_bf16x2(qrc_u32 acc, qrc_u32 x) {
+    qrc_u32 r;
+    asm("{\n\t.reg .b32 t;\n\tabs.bf16x2 t, %2;\n\tmax.bf16x2 %0, %1, t;\n\t}" : "=r"(r) : "r"(acc), "r"(x));
+    return r;
+}
+
+// Streaming 16-byte load: read-only path, no L1 allocation, 256-byte L2 fetch.
+QRC_DEV uint4 ld_stream16(qrc_u64 addr) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(addr));
+    return v;
+}
+
+// Element operators.  Acc starts at +0; to_bits() returns the accumulator as
+// the bit pattern of a non-negative float, so block/grid maxima can use
+// unsigned integer max.
+struct OpAbsF32 {
+    typedef float Acc;
+    static constexpr int kElem = 4;
+    QRC_DEV Acc zero() { return 0.0f; }
+    QRC_DEV Acc step16(Acc a, uint4 v) {
+        a = absmax_step(a, __uint_as_float(v.x)); a = absmax_step(a, __uint_as_float(v.y));
+        a = absmax_step(a, __uint_as_float(v.z)); a = absmax_step(a, __uint_as_float(v.w));
+        return a;
+    }
+    QRC_DEV Acc step_elem(Acc a, qrc_u64 addr) { return absmax_step(a, *(const float*)addr); }
+    QRC_DEV qrc_u32 to_bits(Acc a) { return __float_as_uint(a); }
+};
+
+struct OpAbsBF16 {
+    typedef qrc_u32 Acc;   // two bf16 lanes
+    static constexpr int kElem = 2;
+    QRC_DEV Acc zero() { return 0u; }
+    QRC_DEV Acc step16(Acc a, uint4 v) {
+        a = absmax_step_bf16x2(a, v.x); a = absmax_step_bf16x2(a, v.y);
+        a = absmax_step_bf16x2(a, v.z); a = absmax_step_bf16x2(a, v.w);
+        return a;
+    }
+    QRC_DEV Acc step_elem(Acc a, qrc_u64 addr) {
+        return absmax_step_bf16x2(a, (qrc_u32)(*(const unsigned short*)addr));
+    }
+    QRC_DEV qrc_u32 to_bits(Acc a) {
+        const qrc_u32 lo = a << 16, hi = a & 0xFFFF0000u;   // bf16 -> f32 bits, both >= +0
+        return lo > hi ? lo : hi;
+    }
+};
+
+#ifdef QRC_CHECKED
+// Checked build: every access is tested against [lo, hi) before it is made;
+// a bad one is recorded (first only) and skipped.  Coverage counters record the
+// number of bytes read and an XOR of a hash of every 2-byte unit address read,
+// which the host compares with the same quantities over the input range.
+QRC_DEV qrc_u64 cov_hash(qrc_u64 x) {
+    x ^= x >> 31; x *= 0x7FB5D329728EA185ull; x ^= x >> 27; x *= 0x81DADEF4BC2DD44Dull; x ^= x >> 33;
+    return x;
+}
+struct CheckState { qrc_u64 lo, hi, bytes, xr; qrc_u32* map; };
+QRC_DEV bool check_access(CheckState& cs, qrc_u64 addr, int size) {
+    if (addr < cs.lo || addr + size > cs.hi || (addr & (size - 1))) {
+        if (atomicCAS(&cs.map[H_ERR], 0u, 1u) == 0u) {
+            cs.map[H_ERR_ADDR_LO] = (qrc_u32)addr; cs.map[H_ERR_ADDR_HI] = (qrc_u32)(addr >> 32);
+        }
+        return false;
+    }
+    cs.bytes += size;
+    for (int i = 0; i < size; i += 2) cs.xr ^= cov_hash(addr + i);
+    return true;
+}
+#define QRC_CS_PARAM , CheckState& cs
+#define QRC_CS_ARG , cs
+#define QRC_CHECK(addr, size) if (check_access(cs, (addr), (size)))
+#else
+#define QRC_CS_PARAM
+#define QRC_CS_ARG
+#define QRC_CHECK(addr, size)
+#endif
+
+// Element-wise pass over [x0, x1) by one warp (edges shorter than a pair).
+template <class Op>
+QRC_DEV typename Op::Acc edge_warp(typename Op::Acc acc, qrc_u64 x0, qrc_u64 x1, int lane QRC_CS_PARAM) {
+    for (qrc_u64 x = x0 + (qrc_u64)Op::kElem * lane; x < x1; x += 32ull * Op::kElem) {
+        QRC_CHECK(x, Op::kElem) acc = Op::step_elem(acc, x);
+    }
+    return acc;
+}
+
+// Reads one C-byte chunk (C >= 512) with a warp: lane l reads 16 bytes at
+// l*16 + k*512 for k < C/512; eight loads are kept in flight per lane.
+template <class Op>
+QRC_DEV typename Op::Acc chunk_warp(typename Op::Acc acc, qrc_u64 chunk, int n512, int lane QRC_CS_PARAM) {
+    const qrc_u64 base = chunk + 16ull * lane;
+    for (int k = 0; k < n512; k += 8) {
+        uint4 v[8];
+        #pragma unroll
+        for (int u = 0; u < 8; u++) {
+            v[u] = make_uint4(0u, 0u, 0u, 0u);
+            const qrc_u64 x = base + 512ull * (k + u);
+            if (k + u < n512) { QRC_CHECK(x, 16) v[u] = ld_stream16(x); }
+        }
+        #pragma unroll
+        for (int u = 0; u < 8; u++) acc = Op::step16(acc, v[u]);
+    }
+    return acc;
+}
+
+// scale for an e4m3 per-tensor quantize: 448 / amax with IEEE round-to-nearest
+// division; 1 when amax is 0 (empty / all-zero / all-NaN input) or infinite.
+QRC_DEV float e4m3_scale_from_amax(float amax) {
+    if (!(amax > 0.0f) || amax == __int_as_float(0x7F800000)) return 1.0f;
+    return __fdiv_rn(448.0f, amax);
+}
+
+// Block-wide finish: warp redux, smem, one atomicMax, fenced ticket; the last
+// CTA publishes the result and resets the per-launch scratch.  With `scale_out`
+// it also publishes the e4m3 scale derived from the maximum.
+QRC_DEV void finish_block(qrc_u32 bits, qrc_u32* map, float* out, float* scale_out) {
+    __shared__ qrc_u32 s_w[32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, W = blockDim.x >> 5;
+    bits = __reduce_max_sync(0xFFFFFFFFu, bits);
+    if (lane == 0) s_w[warp] = bits;
+    __syncthreads();
+    if (warp == 0) {
+        qrc_u32 v = lane < W ? s_w[lane] : 0u;
+        v = __reduce_max_sync(0xFFFFFFFFu, v);
+        if (lane == 0) {
+            atomicMax(&map[H_ACC], v);
+            __threadfence();
+            const qrc_u32 t = atomicInc(&map[H_RUN_TICKET], gridDim.x - 1);
+            if (t == gridDim.x - 1) {
+                __threadfence();
+                const qrc_u32 r = atomicExch(&map[H_ACC], 0u);
+                map[H_QUEUE0] = 0u;
+                map[H_QUEUE1] = 0u;
+                out[0] = __uint_as_float(r);
+                if (scale_out) scale_out[0] = e4m3_scale_from_amax(__uint_as_float(r));
+            }
+        }
+    }
+}
+
+// The reduction over n elements at A (element type given by Op).
+template <class Op>
+QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, float* out, float* scale_out, qrc_u32 mode) {
+    const qrc_u64 a = (qrc_u64)A, bytes = n * (qrc_u64)Op::kElem, end = a + bytes;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, W = blockDim.x >> 5;
+    typename Op::Acc acc = Op::zero();
+#ifdef QRC_CHECKED
+    CheckState cs{a, end, 0ull, 0ull, map};
+#endif
+    qrc_u64 lo, hi;   // body [lo, hi); edges [a, lo) and [hi, end)
+
+    if (mode == MODE_STREAM) {
+        // Side-agnostic grid-stride stream over the 16-byte aligned body.
+        lo = (a + 15) & ~15ull; hi = end & ~15ull;
+        if (hi <= lo) { lo = end; hi = end; }
+        const qrc_u64 nv = (hi - lo) / 16;
+        const qrc_u64 tid = (qrc_u64)blockIdx.x * blockDim.x + threadIdx.x;
+        const qrc_u64 stride = (qrc_u64)gridDim.x * blockDim.x;
+        for (qrc_u64 i = tid; i < nv; i += 8 * stride) {
+            uint4 v[8];
+            #pragma unroll
+            for (int u = 0; u < 8; u++) {
+                v[u] = make_uint4(0u, 0u, 0u, 0u);
+                const qrc_u64 j = i + u * stride;
+                if (j < nv) { QRC_CHECK(lo + 16 * j, 16) v[u] = ld_stream16(lo + 16 * j); }
+            }
+            #pragma unroll
+            for (int u = 0; u < 8; u++) acc = Op::step16(acc, v[u]);
+        }
+    } else {
+        // Side-aware pair walk.  Without a valid map for this range it still
+        // runs (mask 0, page bits 0), which splits every pair by halves.
+        const qrc_u64 mb = map_base(map), mbytes = map_bytes(map);
+        const bool aware = map[H_MAGIC] == kMagic && map[H_STATUS] == ST_OK &&
+                           a >= mb && end <= mb + mbytes;
+        const qrc_u64 mask = aware ? map[H_MASK] : 0u;
+        const int clog2 = aware ? (int)map[H_CHUNK_LOG2] : 12;
+        const qrc_u64 C = 1ull << clog2, PAIR = 2 * C;
+        const qrc_u64 page_base = mb & ~(kPage - 1);
+
+        int side;
+        {
+            const qrc_u32 sm = smid();
+            const qrc_u32 lab = (aware && sm < (qrc_u32)kMaxSm) ? map[O_SM_SIDE + sm] : 0u;
+            side = lab ? (int)(lab - 1) : (int)(blockIdx.x & 1);
+        }
+        qrc_u32* queue = &map[side ? H_QUEUE1 : H_QUEUE0];
+
+        lo = (a + PAIR - 1) & ~(PAIR - 1); hi = end & ~(PAIR - 1);
+        if (hi <= lo) { lo = end; hi = end; }
+        const qrc_u64 npairs = (hi - lo) / PAIR;
+        const qrc_u64 ngrabs = (npairs + kPairsPerGrab - 1) / kPairsPerGrab;
+        const int n512 = (int)(C >> 9);
+
+        qrc_u32 g = 0;
+        if (lane == 0) g = atomicAdd(queue, 1u);
+        g = __shfl_sync(0xFFFFFFFFu, g, 0);
+        while ((qrc_u64)g < ngrabs) {
+            qrc_u32 gn = 0;
+            if (lane == 0) gn = atomicAdd(queue, 1u);          // next grab, in flight meanwhile
+            const qrc_u64 p0 = (qrc_u64)g * kPairsPerGrab;
+            const qrc_u64 p1 = p0 + kPairsPerGrab < npairs ? p0 + kPairsPerGrab : npairs;
+            for (qrc_u64 p = p0; p < p1; p++) {
+                const qrc_u64 pa = lo + p * PAIR;
+                int pbit = 0;
+                if (aware && mode != MODE_IGNORE_PAGE_BITS) {
+                    const qrc_u64 pg = (pa - page_base) >> 21;
+                    pbit = (map[O_PAGE_BITS + (pg >> 5)] >> (pg & 31)) & 1;
+                }
+                if (mode == MODE_WRONG_SIDE) pbit ^= 1;
+                const int first_side = parity64(pa & mask) ^ pbit;
+                const qrc_u64 chunk = pa + ((first_side != side) ? C : 0ull);
+                acc = chunk_warp<Op>(acc, chunk, n512, lane QRC_CS_ARG);
+            }
+            g = __shfl_sync(0xFFFFFFFFu, gn, 0);
+        }
+    }
+    // Edges shorter than the body granule: head by CTA 0 warp 0, tail by the
+    // last CTA's last warp.
+    if (blockIdx.x == 0 && warp == 0) acc = edge_warp<Op>(acc, a, lo, lane QRC_CS_ARG);
+    if (blockIdx.x == gridDim.x - 1 && warp == W - 1) acc = edge_warp<Op>(acc, hi, end, lane QRC_CS_ARG);
+
+#ifdef QRC_CHECKED
+    {
+        qrc_u64 b = cs.bytes, x = cs.xr;
+        for (int o = 16; o > 0; o >>= 1) {
+            b += __shfl_xor_sync(0xFFFFFFFFu, b, o);
+            x ^= __shfl_xor_sync(0xFFFFFFFFu, x, o);
+        }
+        if (lane == 0) {
+            atomicAdd((unsigned long long*)&map[H_COV_BYTES_LO], b);
+            atomicXor((unsigned long long*)&map[H_COV_XOR_LO], x);
+        }
+    }
+#endif
+    finish_block(Op::to_bits(acc), map, out, scale_out);
+}
+
+}  // namespace qrc
+
+#ifndef QRC_NO_PLUGIN_ABI
+// ---------------------------------------------------------------------------
+// QuickRunCUDA plugin ABI (QuickRunCUDA.cpp:408-411, :466-474)
+// ---------------------------------------------------------------------------
+extern "C" __global__ void __launch_bounds__(1024, 1)
+init(float* A, unsigned int* side_map, float* C, int num_dwords, int arg1, int arg2) {
+    (void)C; (void)arg1; (void)arg2;
+    qrc::discover(A, num_dwords > 0 ? (qrc_u64)num_dwords * 4ull : 0ull, side_map);
+}
+
+extern "C" __global__ void __launch_bounds__(1024, 1)
+kernel(float* A, unsigned int* side_map, float* C, int num_dwords, int mode, int arg2) {
+    (void)arg2;
+#if defined(FORCE_WRONG_SIDE)
+    mode = qrc::MODE_WRONG_SIDE;
+#elif defined(FORCE_RANDOM_SIDE)
+    mode = qrc::MODE_IGNORE_PAGE_BITS;
+#endif
+    qrc::reduce_run<qrc::OpAbsF32>(A, num_dwords > 0 ? (qrc_u64)num_dwords : 0ull, side_map, C, nullptr,
+                                   (qrc_u32)mode);
+}
+#endif  // QRC_NO_PLUGIN_ABI
+
+#endif  // QRC_SIDE_AWARE_B200_CU
