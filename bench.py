@@ -52,6 +52,8 @@ def parse_args():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-ablation", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=0, help="0 = min(10, max(3, steps // 100))")
+    ap.add_argument("--n-per-gpu", type=int, default=N_PER_GPU,
+                    help="floats per GPU (default 1e9; smaller sizes are for profiling captures)")
     return ap.parse_args()
 
 
@@ -155,7 +157,8 @@ def run_reference(args):
     import numpy as np
     from tests._oracle import Oracle
     orc = Oracle.load()
-    n = N_PER_GPU
+    n = args.n_per_gpu
+    nbytes = 4 * n
     x = orc.uniform_with_outlier(1, n, OUTLIER)
     used = ctypes.c_int()
     fptr = x.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
@@ -168,14 +171,14 @@ def run_reference(args):
         times.append(time.perf_counter() - t0)
     assert r == OUTLIER, r
     total = sum(times)
-    value = BYTES_PER_GPU * len(times) / total / 1e9
+    value = nbytes * len(times) / total / 1e9
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "impl": "reference",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(1e3 * total / len(times), 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": "absmax of 1e9 f32 uniform[-1,1) seed 1 + outlier 7.5 (one GPU's shard)",
-                   "n": n, "bytes": BYTES_PER_GPU},
+                   "n": n, "bytes": nbytes},
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": int(used.value), "kind": "port",
                          "sample": f"full 1e9-float buffer, {args.steps} passes (OpenMP restatement of "
                                    "tests/side_aware.cu:216-219; the reference has no CPU path)"},
@@ -207,16 +210,17 @@ def run_ours(args):
     stream = torch.cuda.current_stream(dev)
 
     # ---- input shard, resident in HBM ----
-    n = N_PER_GPU
+    n = args.n_per_gpu
+    nbytes = 4 * n
     x = torch.empty(n, dtype=torch.float32, device=dev)
     if world == 1:
         seed, offset = 1, 0
         gi, sign = q.outlier(seed, n)
-        workload = "absmax of 1e9 f32 uniform[-1,1) seed 1 + one outlier 7.5 at a seeded index"
+        workload = f"absmax of {n} f32 uniform[-1,1) seed 1 + one outlier 7.5 at a seeded index"
     else:
         seed, offset = 4, rank * n
         gi, sign = q.outlier(seed, world * n)
-        workload = f"sharded absmax: {world} x 1e9 f32 uniform[-1,1) seed 4, one global outlier 7.5, max all-reduce"
+        workload = f"sharded absmax: {world} x {n} f32 uniform[-1,1) seed 4, one global outlier 7.5, max all-reduce"
     q.fill_uniform(x, seed, offset=offset)
     if offset <= gi < offset + n:
         x[gi - offset] = OUTLIER * sign
@@ -260,7 +264,7 @@ def run_ours(args):
     ms_total = float(tmax.item())
     ms_per_step = ms_total / args.steps
     assert out.item() == OUTLIER, f"timed result {out.item()} != {OUTLIER}"
-    value = world * BYTES_PER_GPU / (ms_per_step / 1e3) / 1e9
+    value = world * nbytes / (ms_per_step / 1e3) / 1e9
 
     # ---- ablations on this rank (same kernel, other read modes) ----
     ablation = {}
@@ -277,7 +281,7 @@ def run_ours(args):
             e.record(stream)
             torch.cuda.synchronize()
             assert out.item() == OUTLIER
-            ablation[m] = round(BYTES_PER_GPU / (s.elapsed_time(e) / abl_steps / 1e3) / 1e9, 2)
+            ablation[m] = round(nbytes / (s.elapsed_time(e) / abl_steps / 1e3) / 1e9, 2)
         ctx.mode = args.mode
 
     # ---- end to end through the host-buffer C-ABI call ----
@@ -317,8 +321,8 @@ def run_ours(args):
         if world > 1:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item()) / e2e_steps
-        e2e = {"value": round(world * BYTES_PER_GPU / (e2e_ms / 1e3) / 1e9, 3), "unit": "GB/s",
-               "h2d_bytes_per_step": world * BYTES_PER_GPU, "d2h_bytes_per_step": world * 4,
+        e2e = {"value": round(world * nbytes / (e2e_ms / 1e3) / 1e9, 3), "unit": "GB/s",
+               "h2d_bytes_per_step": world * nbytes, "d2h_bytes_per_step": world * 4,
                "steps": e2e_steps, "ms_per_step": round(e2e_ms, 3),
                "path": "qrc_absmax_f32_host (pinned host -> device staging -> side-aware kernel -> host)"}
         h_ptr = host
@@ -345,24 +349,23 @@ def run_ours(args):
             ts.append(time.perf_counter() - t0)
         assert r == OUTLIER
         med = statistics.median(ts)
-        cpu = {"value": round(BYTES_PER_GPU / med / 1e9, 3), "unit": "GB/s", "cores": int(used.value),
+        cpu = {"value": round(nbytes / med / 1e9, 3), "unit": "GB/s", "cores": int(used.value),
                "kind": "port", "sample": f"the same 1e9-float buffer in host memory, median of {reps} full passes "
                                           "(OpenMP restatement of tests/side_aware.cu:216-219)"}
 
     peak, peak_kind = measured_peak()
-    achieved = BYTES_PER_GPU / (ms_per_step / 1e3) / 1e9 if world == 1 else \
-        BYTES_PER_GPU / (ms_per_step / 1e3) / 1e9
+    achieved = nbytes / (ms_per_step / 1e3) / 1e9
     roofline = {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "peak_source": peak_kind,
                 "traffic": profile_traffic("absmax_f32_1e9_side_aware"),
-                "algorithmic_bytes_per_launch": BYTES_PER_GPU,
+                "algorithmic_bytes_per_launch": nbytes,
                 "kernel": "qrc_k_absmax_f32<1024>"}
 
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": max(args.warmup, 3), "ms_per_step": round(ms_per_step, 5), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": workload, "n_per_gpu": n, "bytes_per_gpu": BYTES_PER_GPU, "mode": args.mode,
+        "config": {"workload": workload, "n_per_gpu": n, "bytes_per_gpu": nbytes, "mode": args.mode,
                    "launch": f"{info['num_sms_measured'] or ''} SMs x 1 CTA x 1024 threads",
                    "l2": L2_NOTE, "parallelism": "replicated shards" if world == 1 else f"shard{world}+nccl_max_allreduce"},
         "roofline": roofline,

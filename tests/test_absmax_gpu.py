@@ -109,7 +109,7 @@ def test_absmax_outlier_positions(buf, oracle):
     ([float("nan")] * 7, 0),
     ([-0.0] * 9, 0),
     ([0.5, float("inf"), float("nan")], 0x7F800000),
-    ([1e-45, -2e-45, 0.0], 2),           # denormals are kept (no flush)
+    ([1.401298464324817e-45, -2.802596928649634e-45, 0.0], 2),   # denormals kept: bits 1, 2
     ([float("nan"), -3.0, 2.0], 0x40400000),
 ])
 def test_absmax_special_values(cuda, qrc, oracle, vals, expect_bits):
