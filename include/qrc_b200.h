@@ -112,6 +112,17 @@ int qrc_ctx_set_mode(qrc_ctx* ctx, int mode);
  * the reference's `-p -t 1024` (QuickRunCUDA.cpp:365-369). */
 int qrc_ctx_set_launch(qrc_ctx* ctx, int blocks_per_sm, int threads_per_block);
 
+/* Load pipeline for later reductions.  0 (default): each warp keeps eight
+ * 16-byte loads per lane in flight in registers (128 KiB per SM at 1024
+ * threads).  2..16: each warp stages its chunks through that many 4 KiB
+ * shared-memory slots filled by 1-D bulk async copies (cp.async.bulk with
+ * mbarrier completion), so up to threads/32 * slots * 4 KiB per SM are in
+ * flight without registers; needs blocks_per_sm == 1 and
+ * threads/32 * slots * 4104 <= 227 KiB (e.g. 256 threads x 6 slots).
+ * No reference counterpart (the reference uses register loads only,
+ * tests/side_aware.cu:319-325). */
+int qrc_ctx_set_pipeline(qrc_ctx* ctx, int bulk_slots_per_warp);
+
 /* *d_out = max_i |d_in[i]| over n floats (IEEE maxNum: NaN inputs are ignored,
  * -0 gives +0, n == 0 gives +0).  d_in must be 4-byte aligned; the side-aware
  * path applies when [d_in, d_in + n) lies inside the context's buffer.

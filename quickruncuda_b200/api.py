@@ -120,6 +120,11 @@ class SideAwareContext:
         nat.check(self.lib, "qrc_ctx_set_launch",
                   self.lib.qrc_ctx_set_launch(self.handle, blocks_per_sm, threads))
 
+    def set_pipeline(self, bulk_slots_per_warp: int) -> None:
+        """0: register loads; >= 2: bulk-copy staging slots per warp."""
+        nat.check(self.lib, "qrc_ctx_set_pipeline",
+                  self.lib.qrc_ctx_set_pipeline(self.handle, bulk_slots_per_warp))
+
     # -- work --------------------------------------------------------------
     def absmax(self, x, out=None, n: Optional[int] = None, stream=None):
         """max |x| of a float32 CUDA tensor (or raw pointer + n) into `out`

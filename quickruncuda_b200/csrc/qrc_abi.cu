@@ -120,14 +120,20 @@ thread_local int g_last_cuda = 0;
         if (e_ != cudaSuccess) { g_last_cuda = (int)e_; return QRC_ERR_CUDA; } \
     } while (0)
 
-// Makes `dev` current for the scope and restores the caller's device.
+// Makes `dev` current for the scope and restores the caller's device.  When
+// `dev` is already current nothing is touched, so a context the caller made
+// current through the driver API (as the QuickRunCUDA harness does with
+// cuCtxCreate) stays current.
 struct DeviceScope {
-    int prev = -1, ok = 0;
+    int prev = -1;
+    bool ok = false, switched = false;
     explicit DeviceScope(int dev) {
-        if (cudaGetDevice(&prev) != cudaSuccess) { prev = -1; }
-        ok = (prev == dev) || (cudaSetDevice(dev) == cudaSuccess);
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev == dev) { ok = true; return; }
+        ok = cudaSetDevice(dev) == cudaSuccess;
+        switched = ok && prev >= 0;
     }
-    ~DeviceScope() { if (prev >= 0) cudaSetDevice(prev); }
+    ~DeviceScope() { if (switched) cudaSetDevice(prev); }
 };
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
@@ -142,6 +148,7 @@ struct qrc_ctx {
     int mode = QRC_MODE_SIDE_AWARE;
     int blocks_per_sm = 1;
     int threads = 1024;
+    int bulk_slots = 0;             // 0: register loads; >= 2: bulk-copy staging slots per warp
     const void* base = nullptr;
     size_t bytes = 0;
     qrc_u32* d_map = nullptr;
@@ -172,13 +179,35 @@ static void fill_info(qrc_ctx* c, const qrc_u32* h) {
     i.discover_smid = h[qrc::H_SMID_LAST];
 }
 
+// Dynamic shared memory of a launch: the bulk staging ring when enabled.
+static size_t launch_smem(const qrc_ctx* c) {
+    return c->bulk_slots ? (size_t)(c->threads / 32) * c->bulk_slots * qrc::kSlotStride : 0;
+}
+
+template <int T>
+static cudaError_t allow_smem(size_t smem) {
+    static size_t granted_f32 = 0, granted_bf16 = 0;   // per process; device-independent attribute
+    if (smem > granted_f32) {
+        cudaError_t e = cudaFuncSetAttribute(qrc_k_absmax_f32<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        granted_f32 = smem;
+    }
+    if (smem > granted_bf16) {
+        cudaError_t e = cudaFuncSetAttribute(qrc_k_amax_bf16<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        granted_bf16 = smem;
+    }
+    return cudaSuccess;
+}
+
 static int launch_absmax(qrc_ctx* c, const float* in, size_t n, float* out, cudaStream_t s) {
     const int grid = c->num_sms * c->blocks_per_sm;
     const qrc_u32 mode = (qrc_u32)c->mode;
+    const size_t smem = launch_smem(c);
     switch (c->threads) {
-        case 1024: qrc_k_absmax_f32<1024><<<grid, 1024, 0, s>>>(in, n, c->d_map, out, mode); break;
-        case 512:  qrc_k_absmax_f32<512><<<grid, 512, 0, s>>>(in, n, c->d_map, out, mode); break;
-        default:   qrc_k_absmax_f32<256><<<grid, 256, 0, s>>>(in, n, c->d_map, out, mode); break;
+        case 1024: QRC_CK(allow_smem<1024>(smem)); qrc_k_absmax_f32<1024><<<grid, 1024, smem, s>>>(in, n, c->d_map, out, mode); break;
+        case 512:  QRC_CK(allow_smem<512>(smem)); qrc_k_absmax_f32<512><<<grid, 512, smem, s>>>(in, n, c->d_map, out, mode); break;
+        default:   QRC_CK(allow_smem<256>(smem)); qrc_k_absmax_f32<256><<<grid, 256, smem, s>>>(in, n, c->d_map, out, mode); break;
     }
     QRC_CK(cudaGetLastError());
     return QRC_OK;
@@ -261,9 +290,22 @@ QRC_API int qrc_ctx_set_mode(qrc_ctx* c, int mode) {
 QRC_API int qrc_ctx_set_launch(qrc_ctx* c, int blocks_per_sm, int threads) {
     if (!c || (threads != 256 && threads != 512 && threads != 1024)) return QRC_ERR_INVALID;
     if (blocks_per_sm < 1 || blocks_per_sm * threads > 2048) return QRC_ERR_INVALID;
+    if (c->bulk_slots && (blocks_per_sm != 1 || (size_t)(threads / 32) * c->bulk_slots * qrc::kSlotStride > 227 * 1024))
+        return QRC_ERR_INVALID;
     c->blocks_per_sm = blocks_per_sm;
     c->threads = threads;
     if (c->stage_ctx) qrc_ctx_set_launch(c->stage_ctx, blocks_per_sm, threads);
+    return QRC_OK;
+}
+
+QRC_API int qrc_ctx_set_pipeline(qrc_ctx* c, int slots) {
+    if (!c || slots < 0 || slots == 1 || slots > 16) return QRC_ERR_INVALID;
+    if (slots) {
+        const size_t smem = (size_t)(c->threads / 32) * slots * qrc::kSlotStride;
+        if (smem > 227 * 1024 || c->blocks_per_sm != 1) return QRC_ERR_INVALID;
+    }
+    c->bulk_slots = slots;
+    if (c->stage_ctx) c->stage_ctx->bulk_slots = slots;
     return QRC_OK;
 }
 
@@ -290,6 +332,7 @@ QRC_API int qrc_absmax_f32_host(const float* h_in, size_t n, float* h_out, qrc_c
         c->stage_ctx->mode = c->mode;
         c->stage_ctx->blocks_per_sm = c->blocks_per_sm;
         c->stage_ctx->threads = c->threads;
+        c->stage_ctx->bulk_slots = c->bulk_slots;
     }
     qrc_ctx* sc = c->stage_ctx ? c->stage_ctx : c;
     if (n) QRC_CK(cudaMemcpyAsync(c->d_stage, h_in, n * sizeof(float), cudaMemcpyHostToDevice, s));
@@ -308,10 +351,11 @@ QRC_API int qrc_amax_quant_e4m3(const uint16_t* d_in, size_t n, uint8_t* d_q, fl
     cudaStream_t s = as_stream(stream);
     float* amax = d_amax ? d_amax : c->d_scalars;
     const int grid = c->num_sms * c->blocks_per_sm;
+    const size_t smem = launch_smem(c);
     switch (c->threads) {
-        case 1024: qrc_k_amax_bf16<1024><<<grid, 1024, 0, s>>>(d_in, n, c->d_map, amax, d_scale, c->mode); break;
-        case 512:  qrc_k_amax_bf16<512><<<grid, 512, 0, s>>>(d_in, n, c->d_map, amax, d_scale, c->mode); break;
-        default:   qrc_k_amax_bf16<256><<<grid, 256, 0, s>>>(d_in, n, c->d_map, amax, d_scale, c->mode); break;
+        case 1024: QRC_CK(allow_smem<1024>(smem)); qrc_k_amax_bf16<1024><<<grid, 1024, smem, s>>>(d_in, n, c->d_map, amax, d_scale, c->mode); break;
+        case 512:  QRC_CK(allow_smem<512>(smem)); qrc_k_amax_bf16<512><<<grid, 512, smem, s>>>(d_in, n, c->d_map, amax, d_scale, c->mode); break;
+        default:   QRC_CK(allow_smem<256>(smem)); qrc_k_amax_bf16<256><<<grid, 256, smem, s>>>(d_in, n, c->d_map, amax, d_scale, c->mode); break;
     }
     QRC_CK(cudaGetLastError());
     if (n) {

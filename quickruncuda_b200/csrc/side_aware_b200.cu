@@ -73,6 +73,7 @@ typedef unsigned int qrc_u32;
 typedef unsigned long long qrc_u64;
 
 #define QRC_DEV static __device__ __forceinline__
+#define QRC_MEMBER __device__ __forceinline__
 
 namespace qrc {
 
@@ -80,7 +81,19 @@ constexpr qrc_u32 kMagic = 0x51525341u;         // 'QRSA'
 constexpr qrc_u64 kPage = 2ull * 1024 * 1024;   // side bit granularity (2 MiB pages)
 constexpr int kProbeIters = 32;                  // dependent atomics per latency probe
 constexpr int kMaxSm = 256;
-constexpr qrc_u32 kPairsPerGrab = 8;             // pairs a warp takes per queue atomic
+// Compile-time knobs (a kernel-file user can set them with the harness' -H,
+// like the reference's own #defines):
+//   QRC_MAX_GRAB   most pairs a warp takes per queue atomic (guided: grabs
+//                  shrink to 1 pair as its side's queue empties)
+//   QRC_LOAD_KIND  0 ld.global.v4, 1 ld.global.nc.L1::no_allocate.L2::256B.v4,
+//                  2 as 1 plus L2::evict_first, 3 256-bit ld.global.nc.v8
+#ifndef QRC_MAX_GRAB
+#define QRC_MAX_GRAB 8
+#endif
+#ifndef QRC_LOAD_KIND
+#define QRC_LOAD_KIND 1
+#endif
+constexpr qrc_u32 kMaxGrab = QRC_MAX_GRAB;
 constexpr int kVerifyRandom = 64;
 constexpr int kVerifyCal = 8;                    // anchor + partner re-probes in verification
 constexpr int kCalProbes = 16;                   // per side, calibration wave
@@ -95,7 +108,7 @@ enum : qrc_u32 {
     H_RUN_TICKET = 17, H_ACC = 18, H_PAGE_WORDS_CAP = 19, H_MASK_MEASURED = 20,
     H_SM_C0 = 21, H_SM_C1 = 22, H_BIT_C0 = 23, H_BIT_C1 = 24, H_SMID_LAST = 25,
     H_QUEUE0 = 32, H_QUEUE1 = 64,                  // each on its own 128-byte line
-    H_ERR = 96, H_ERR_ADDR_LO = 97, H_ERR_ADDR_HI = 98,
+    H_ERR = 96, H_ERR_ADDR_LO = 97, H_ERR_ADDR_HI = 98, H_WAIT_ERR = 99,
     H_COV_BYTES_LO = 100, H_COV_BYTES_HI = 101, H_COV_XOR_LO = 102, H_COV_XOR_HI = 103,
     O_BITLAT = 128,                                // 21 raw latencies of the mask probes
     O_SM_SIDE = 256,                               // per SM: 0 unknown, 1 side 0, 2 side 1
@@ -402,13 +415,31 @@ QRC_DEV qrc_u32 absmax_step_bf16x2(qrc_u32 acc, qrc_u32 x) {
     return r;
 }
 
-// Streaming 16-byte load: read-only path, no L1 allocation, 256-byte L2 fetch.
+// Streaming 16-byte load (flavour chosen by QRC_LOAD_KIND).
 QRC_DEV uint4 ld_stream16(qrc_u64 addr) {
     uint4 v;
+#if QRC_LOAD_KIND == 0
+    asm volatile("ld.global.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(addr));
+#elif QRC_LOAD_KIND == 2
+    asm volatile("{\n\t.reg .b64 pol;\n\tcreatepolicy.fractional.L2::evict_first.b64 pol, 1.0;\n\t"
+                 "ld.global.nc.L1::no_allocate.L2::cache_hint.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4], pol;\n\t}"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(addr));
+#else
     asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"
                  : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(addr));
+#endif
     return v;
 }
+
+#if QRC_LOAD_KIND == 3
+// 32-byte load (sm_100 256-bit global loads), as two uint4.
+QRC_DEV void ld_stream32(qrc_u64 addr, uint4& a, uint4& b) {
+    asm volatile("ld.global.nc.L1::no_allocate.L2::evict_first.L2::256B.v8.u32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(a.x), "=r"(a.y), "=r"(a.z), "=r"(a.w), "=r"(b.x), "=r"(b.y), "=r"(b.z), "=r"(b.w)
+                 : "l"(addr));
+}
+#endif
 
 // Element operators.  Acc starts at +0; to_bits() returns the accumulator as
 // the bit pattern of a non-negative float, so block/grid maxima can use
@@ -484,9 +515,27 @@ QRC_DEV typename Op::Acc edge_warp(typename Op::Acc acc, qrc_u64 x0, qrc_u64 x1,
 }
 
 // Reads one C-byte chunk (C >= 512) with a warp: lane l reads 16 bytes at
-// l*16 + k*512 for k < C/512; eight loads are kept in flight per lane.
+// l*16 + k*512 for k < C/512 (or, with 256-bit loads, 32 bytes at
+// l*32 + k*1024); eight 16-byte loads' worth are kept in flight per lane.
 template <class Op>
 QRC_DEV typename Op::Acc chunk_warp(typename Op::Acc acc, qrc_u64 chunk, int n512, int lane QRC_CS_PARAM) {
+#if QRC_LOAD_KIND == 3 && !defined(QRC_CHECKED)
+    if (n512 >= 2) {
+        const qrc_u64 base = chunk + 32ull * lane;
+        const int n1k = n512 >> 1;
+        for (int k = 0; k < n1k; k += 4) {
+            uint4 v[8];
+            #pragma unroll
+            for (int u = 0; u < 4; u++) {
+                v[2 * u] = v[2 * u + 1] = make_uint4(0u, 0u, 0u, 0u);
+                if (k + u < n1k) ld_stream32(base + 1024ull * (k + u), v[2 * u], v[2 * u + 1]);
+            }
+            #pragma unroll
+            for (int u = 0; u < 8; u++) acc = Op::step16(acc, v[u]);
+        }
+        return acc;
+    }
+#endif
     const qrc_u64 base = chunk + 16ull * lane;
     for (int k = 0; k < n512; k += 8) {
         uint4 v[8];
@@ -527,9 +576,10 @@ QRC_DEV void finish_block(qrc_u32 bits, qrc_u32* map, float* out, float* scale_o
             const qrc_u32 t = atomicInc(&map[H_RUN_TICKET], gridDim.x - 1);
             if (t == gridDim.x - 1) {
                 __threadfence();
-                const qrc_u32 r = atomicExch(&map[H_ACC], 0u);
+                qrc_u32 r = atomicExch(&map[H_ACC], 0u);
                 map[H_QUEUE0] = 0u;
                 map[H_QUEUE1] = 0u;
+                if (map[H_WAIT_ERR]) r = 0x7FFFFFFFu;   // a bounded wait gave up: no valid maximum
                 out[0] = __uint_as_float(r);
                 if (scale_out) scale_out[0] = e4m3_scale_from_amax(__uint_as_float(r));
             }
@@ -537,7 +587,218 @@ QRC_DEV void finish_block(qrc_u32 bits, qrc_u32* map, float* out, float* scale_o
     }
 }
 
-// The reduction over n elements at A (element type given by Op).
+// Per-warp walk over the pairs of one side.  Built from the side map (or
+// without one: mask 0, page bits 0), it hands each call the address of the
+// next C-byte chunk this warp must read.  Work comes from the side's queue, a
+// counter of pairs: a warp adds its grab size and owns the pairs between the
+// old and new value.  Grabs are guided: QRC_MAX_GRAB pairs while plenty are
+// left, shrinking to one pair as the queue empties, so all warps of a side
+// finish within about one chunk of each other.  The next grab is requested
+// while the current one is read.  All lanes call next() together (it
+// broadcasts lane 0's atomics).
+struct SideWalk {
+    qrc_u64 lo, hi, C, mask, page_base, npairs, p, p1, nstart;
+    const qrc_u32* page_bits;
+    qrc_u32* queue;
+    qrc_u32 nsize, spread;
+    int side, use_page_bits, flip;
+    bool pending;
+
+    QRC_MEMBER void setup(qrc_u64 a, qrc_u64 end, qrc_u32* map, qrc_u32 mode) {
+        const qrc_u64 mb = map_base(map), mbytes = map_bytes(map);
+        const bool aware = map[H_MAGIC] == kMagic && map[H_STATUS] == ST_OK && a >= mb && end <= mb + mbytes;
+        mask = aware ? map[H_MASK] : 0u;
+        C = 1ull << (aware ? (int)map[H_CHUNK_LOG2] : 12);
+        page_base = mb & ~(kPage - 1);
+        page_bits = map + O_PAGE_BITS;
+        use_page_bits = aware && mode != MODE_IGNORE_PAGE_BITS;
+        flip = mode == MODE_WRONG_SIDE;
+        const qrc_u32 sm = smid();
+        const qrc_u32 lab = (aware && sm < (qrc_u32)kMaxSm) ? map[O_SM_SIDE + sm] : 0u;
+        side = lab ? (int)(lab - 1) : (int)(blockIdx.x & 1);
+        queue = &map[side ? H_QUEUE1 : H_QUEUE0];
+        const qrc_u64 PAIR = 2 * C;
+        lo = (a + PAIR - 1) & ~(PAIR - 1);
+        hi = end & ~(PAIR - 1);
+        if (hi <= lo) { lo = end; hi = end; }
+        npairs = (hi - lo) / PAIR;
+        spread = gridDim.x * (blockDim.x >> 5);     // ~2x the warps reading one side
+        p = p1 = nstart = 0;
+        nsize = 0;
+        pending = false;
+    }
+    // Grab size when `seen` pairs of this side are already taken.
+    QRC_MEMBER qrc_u32 grab_size(qrc_u64 seen) const {
+        const qrc_u64 left = npairs > seen ? npairs - seen : 0;
+        const qrc_u64 s = left / spread;
+        return s >= kMaxGrab ? kMaxGrab : (s < 1 ? 1u : (qrc_u32)s);
+    }
+    // Lane 0 requests the grab that follows [start, start + size); the reply
+    // is read by the next call that runs out of pairs.
+    QRC_MEMBER void request(int lane, qrc_u64 start, qrc_u32 size) {
+        if (lane == 0) {
+            nsize = grab_size(start + size);
+            nstart = atomicAdd(queue, nsize);
+        }
+        pending = true;
+    }
+    // Makes [st, st + sz) current; returns false when the queue is exhausted.
+    QRC_MEMBER bool adopt(int lane, qrc_u64 st, qrc_u32 sz) {
+        if (st >= npairs) { p = p1 = 0; pending = false; return false; }
+        p = st;
+        p1 = st + sz < npairs ? st + sz : npairs;
+        request(lane, st, sz);
+        return true;
+    }
+    QRC_MEMBER void begin(int lane) {
+        const qrc_u32 sz = grab_size(0);
+        qrc_u64 st = 0;
+        if (lane == 0) st = atomicAdd(queue, sz);
+        st = __shfl_sync(0xFFFFFFFFu, st, 0);
+        adopt(lane, st, sz);
+    }
+    QRC_MEMBER qrc_u64 next(int lane) {
+        if (p >= p1) {
+            if (!pending) return 0;
+            const qrc_u64 st = __shfl_sync(0xFFFFFFFFu, nstart, 0);
+            const qrc_u32 sz = __shfl_sync(0xFFFFFFFFu, nsize, 0);
+            if (!adopt(lane, st, sz)) return 0;
+        }
+        const qrc_u64 pa = lo + p * (2 * C);
+        p++;
+        int pbit = 0;
+        if (use_page_bits) {
+            const qrc_u64 pg = (pa - page_base) >> 21;
+            pbit = (page_bits[pg >> 5] >> (pg & 31)) & 1;
+        }
+        const int first_side = parity64(pa & mask) ^ pbit ^ flip;
+        return pa + ((first_side != side) ? C : 0ull);
+    }
+};
+
+// ---- bulk-copy staging (cp.async.bulk global -> shared, mbarrier completion) ----
+
+QRC_DEV void mbar_init(qrc_u32 bar, qrc_u32 count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(bar), "r"(count) : "memory");
+}
+QRC_DEV void mbar_arrive_expect_tx(qrc_u32 bar, qrc_u32 bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(bar), "r"(bytes) : "memory");
+}
+QRC_DEV bool mbar_try_wait(qrc_u32 bar, qrc_u32 parity) {
+    qrc_u32 ok;
+    asm volatile("{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+                 "selp.u32 %0, 1, 0, p;\n\t}" : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+    return ok != 0;
+}
+// Waits for the phase with the given parity to complete; gives up after
+// kWaitCycles SM clocks and returns false.
+constexpr long long kWaitCycles = 1ll << 31;   // about one second
+QRC_DEV bool mbar_wait_bounded(qrc_u32 bar, qrc_u32 parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    while (!mbar_try_wait(bar, parity))
+        if (clock64() - t0 > kWaitCycles) return false;
+    return true;
+}
+QRC_DEV void bulk_g2s(qrc_u32 dst, qrc_u64 src, qrc_u32 bytes, qrc_u32 bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 :: "r"(dst), "l"(src), "r"(bytes), "r"(bar) : "memory");
+}
+QRC_DEV void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+QRC_DEV void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+
+constexpr qrc_u32 kSlotBytes = 4096;                  // one staging slot
+constexpr qrc_u32 kSlotStride = kSlotBytes + 8;       // slot + its mbarrier, for sizing
+QRC_DEV int bulk_slots_per_warp(qrc_u32 dyn_smem_bytes, int warps) {
+    const int s = (int)(dyn_smem_bytes / ((qrc_u32)warps * kSlotStride));
+    return s > 16 ? 16 : s;
+}
+QRC_DEV qrc_u32 dynamic_smem_size() {
+    qrc_u32 r;
+    asm volatile("mov.u32 %0, %%dynamic_smem_size;" : "=r"(r));
+    return r;
+}
+
+// Bulk variant of the side-aware walk: each warp owns S slots of 4 KiB in
+// dynamic shared memory with one mbarrier each; lane 0 keeps every slot
+// filled with the warp's next chunk through cp.async.bulk (one 1-D copy per
+// slot, no multicast), all lanes wait for the slot, reduce it from shared
+// memory and hand it back.  Up to warps * S * 4 KiB per SM are in flight
+// without using registers.  Waits are bounded: on a timeout the warp records
+// H_WAIT_ERR, drains its own copies (again bounded) and stops; the launch then
+// publishes NaN instead of a maximum.
+template <class Op>
+QRC_DEV typename Op::Acc bulk_walk(typename Op::Acc acc, SideWalk& w, int S, qrc_u32* map, int lane, int warp) {
+    extern __shared__ __align__(128) unsigned char qrc_dsmem[];
+    const int W = blockDim.x >> 5;
+    const qrc_u32 U = w.C < kSlotBytes ? (qrc_u32)w.C : kSlotBytes;   // bytes per copy
+    const int per_chunk = (int)(w.C / U);
+    const qrc_u32 slots = (qrc_u32)__cvta_generic_to_shared(qrc_dsmem) + (qrc_u32)(warp * S) * kSlotBytes;
+    const qrc_u32 bars = (qrc_u32)__cvta_generic_to_shared(qrc_dsmem) + (qrc_u32)(W * S) * kSlotBytes + (qrc_u32)(warp * S) * 8u;
+    if (lane == 0) {
+        for (int s = 0; s < S; s++) mbar_init(bars + 8u * s, 1);
+        fence_mbar_init();
+        fence_proxy_async_smem();
+    }
+    __syncwarp();
+
+    qrc_u64 chunk = 0;
+    int k = per_chunk;
+    auto next_unit = [&]() -> qrc_u64 {
+        if (k == per_chunk) { chunk = w.next(lane); k = 0; }
+        if (!chunk) return 0;
+        return chunk + (qrc_u64)(k++) * U;
+    };
+    w.begin(lane);
+    qrc_u32 valid = 0, parity = 0;
+    for (int s = 0; s < S; s++) {
+        const qrc_u64 src = next_unit();
+        if (!src) break;
+        valid |= 1u << s;
+        if (lane == 0) { mbar_arrive_expect_tx(bars + 8u * s, U); bulk_g2s(slots + s * kSlotBytes, src, U, bars + 8u * s); }
+    }
+    int s = 0;
+    bool failed = false;
+    const int n512 = (int)(U >> 9);
+    while (valid) {
+        if (valid & (1u << s)) {
+            if (!mbar_wait_bounded(bars + 8u * s, (parity >> s) & 1u)) { failed = true; break; }
+            parity ^= 1u << s;
+            const unsigned char* sp = qrc_dsmem + (size_t)(warp * S + s) * kSlotBytes + 16 * lane;
+            if (n512 == 8) {
+                uint4 v[8];
+                #pragma unroll
+                for (int u = 0; u < 8; u++) v[u] = *(const uint4*)(sp + 512 * u);
+                #pragma unroll
+                for (int u = 0; u < 8; u++) acc = Op::step16(acc, v[u]);
+            } else {
+                for (int u = 0; u < n512; u++) acc = Op::step16(acc, *(const uint4*)(sp + 512 * u));
+            }
+            __syncwarp();
+            const qrc_u64 src = next_unit();
+            if (src) {
+                if (lane == 0) {
+                    fence_proxy_async_smem();       // our generic reads of the slot before the async refill
+                    mbar_arrive_expect_tx(bars + 8u * s, U);
+                    bulk_g2s(slots + s * kSlotBytes, src, U, bars + 8u * s);
+                }
+            } else {
+                valid &= ~(1u << s);
+            }
+        }
+        s = (s + 1 == S) ? 0 : s + 1;
+    }
+    if (failed) {
+        if (lane == 0) atomicOr(&map[H_WAIT_ERR], 1u);
+        for (int t = 0; t < S; t++)                     // drain this warp's copies, bounded
+            if (valid & (1u << t)) mbar_wait_bounded(bars + 8u * t, (parity >> t) & 1u);
+    }
+    return acc;
+}
+
+// The reduction over n elements at A (element type given by Op).  Uses the
+// bulk staging when the launch provides dynamic shared memory for at least two
+// slots per warp, register loads otherwise.
 template <class Op>
 QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, float* out, float* scale_out, qrc_u32 mode) {
     const qrc_u64 a = (qrc_u64)A, bytes = n * (qrc_u64)Op::kElem, end = a + bytes;
@@ -567,51 +828,20 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, float* out, floa
             for (int u = 0; u < 8; u++) acc = Op::step16(acc, v[u]);
         }
     } else {
-        // Side-aware pair walk.  Without a valid map for this range it still
-        // runs (mask 0, page bits 0), which splits every pair by halves.
-        const qrc_u64 mb = map_base(map), mbytes = map_bytes(map);
-        const bool aware = map[H_MAGIC] == kMagic && map[H_STATUS] == ST_OK &&
-                           a >= mb && end <= mb + mbytes;
-        const qrc_u64 mask = aware ? map[H_MASK] : 0u;
-        const int clog2 = aware ? (int)map[H_CHUNK_LOG2] : 12;
-        const qrc_u64 C = 1ull << clog2, PAIR = 2 * C;
-        const qrc_u64 page_base = mb & ~(kPage - 1);
-
-        int side;
+        SideWalk w;
+        w.setup(a, end, map, mode);
+        lo = w.lo; hi = w.hi;
+        const int S = bulk_slots_per_warp(dynamic_smem_size(), W);
+#ifndef QRC_CHECKED
+        if (S >= 2) {
+            acc = bulk_walk<Op>(acc, w, S, map, lane, warp);
+        } else
+#endif
         {
-            const qrc_u32 sm = smid();
-            const qrc_u32 lab = (aware && sm < (qrc_u32)kMaxSm) ? map[O_SM_SIDE + sm] : 0u;
-            side = lab ? (int)(lab - 1) : (int)(blockIdx.x & 1);
-        }
-        qrc_u32* queue = &map[side ? H_QUEUE1 : H_QUEUE0];
-
-        lo = (a + PAIR - 1) & ~(PAIR - 1); hi = end & ~(PAIR - 1);
-        if (hi <= lo) { lo = end; hi = end; }
-        const qrc_u64 npairs = (hi - lo) / PAIR;
-        const qrc_u64 ngrabs = (npairs + kPairsPerGrab - 1) / kPairsPerGrab;
-        const int n512 = (int)(C >> 9);
-
-        qrc_u32 g = 0;
-        if (lane == 0) g = atomicAdd(queue, 1u);
-        g = __shfl_sync(0xFFFFFFFFu, g, 0);
-        while ((qrc_u64)g < ngrabs) {
-            qrc_u32 gn = 0;
-            if (lane == 0) gn = atomicAdd(queue, 1u);          // next grab, in flight meanwhile
-            const qrc_u64 p0 = (qrc_u64)g * kPairsPerGrab;
-            const qrc_u64 p1 = p0 + kPairsPerGrab < npairs ? p0 + kPairsPerGrab : npairs;
-            for (qrc_u64 p = p0; p < p1; p++) {
-                const qrc_u64 pa = lo + p * PAIR;
-                int pbit = 0;
-                if (aware && mode != MODE_IGNORE_PAGE_BITS) {
-                    const qrc_u64 pg = (pa - page_base) >> 21;
-                    pbit = (map[O_PAGE_BITS + (pg >> 5)] >> (pg & 31)) & 1;
-                }
-                if (mode == MODE_WRONG_SIDE) pbit ^= 1;
-                const int first_side = parity64(pa & mask) ^ pbit;
-                const qrc_u64 chunk = pa + ((first_side != side) ? C : 0ull);
+            const int n512 = (int)(w.C >> 9);
+            w.begin(lane);
+            for (qrc_u64 chunk = w.next(lane); chunk; chunk = w.next(lane))
                 acc = chunk_warp<Op>(acc, chunk, n512, lane QRC_CS_ARG);
-            }
-            g = __shfl_sync(0xFFFFFFFFu, gn, 0);
         }
     }
     // Edges shorter than the body granule: head by CTA 0 warp 0, tail by the

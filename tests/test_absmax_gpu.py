@@ -9,7 +9,8 @@ SIZES = [0, 1, 3, 4, 5, 1023, 4096, 8191, 8193, (1 << 19) - 1, (1 << 19) + 1,
          (2 * MIB) // 4 - 1, (2 * MIB) // 4, (2 * MIB) // 4 + 1, 3 * MIB + 7]
 OFFSETS = [0, 1, 3, 1021]          # floats into the context's buffer
 MODES = [0, 1, 2, 3]
-SHAPES = [(1, 1024), (2, 512), (4, 256)]
+# (blocks per SM, threads per block, bulk slots per warp; 0 = register loads)
+SHAPES = [(1, 1024, 0), (2, 512, 0), (4, 256, 0), (1, 256, 6), (1, 512, 3), (1, 256, 2)]
 
 
 def _bits(t):
@@ -68,7 +69,9 @@ def test_absmax_parity_sizes_offsets(buf, oracle, mode, shape):
     import torch
     x, ctx = buf
     ctx.mode = mode
-    ctx.set_launch(*shape)
+    ctx.set_pipeline(0)
+    ctx.set_launch(shape[0], shape[1])
+    ctx.set_pipeline(shape[2])
     host = x.cpu().numpy()
     out = torch.empty(1, dtype=torch.float32, device=x.device)
     for off in OFFSETS:
@@ -78,7 +81,46 @@ def test_absmax_parity_sizes_offsets(buf, oracle, mode, shape):
             want = oracle.absmax_bits(host[off:off + n])
             assert got == want, (mode, shape, off, n, hex(got), hex(want))
     ctx.mode = 0
+    ctx.set_pipeline(0)
     ctx.set_launch(1, 1024)
+
+
+def test_pipeline_argument_checks(buf):
+    x, ctx = buf
+    import quickruncuda_b200 as q
+    with pytest.raises(q.QrcError):
+        ctx.set_pipeline(1)              # a ring needs at least two slots
+    with pytest.raises(q.QrcError):
+        ctx.set_pipeline(6)              # 1024 threads x 6 slots exceeds shared memory
+    ctx.set_launch(1, 256)
+    ctx.set_pipeline(6)
+    with pytest.raises(q.QrcError):
+        ctx.set_launch(2, 256)           # two CTAs per SM cannot both hold the ring
+    ctx.set_pipeline(0)
+    ctx.set_launch(1, 1024)
+
+
+def test_bulk_pipeline_full_buffer_and_outliers(buf, oracle):
+    import torch
+    x, ctx = buf
+    ctx.set_launch(1, 256)
+    ctx.set_pipeline(6)
+    saved = x[-1].clone()
+    try:
+        for mode in MODES:
+            ctx.mode = mode
+            for p in (0, 4095, 4096, x.numel() - 1):
+                old = x[p].clone()
+                x[p] = 1e30
+                assert ctx.absmax(x).item() == np.float32(1e30), (mode, p)
+                x[p] = old
+        m = ctx.read_map(128)
+        assert m[99] == 0                # no bounded wait gave up
+    finally:
+        x[-1] = saved
+        ctx.mode = 0
+        ctx.set_pipeline(0)
+        ctx.set_launch(1, 1024)
 
 
 def test_absmax_outlier_positions(buf, oracle):

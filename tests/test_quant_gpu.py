@@ -79,6 +79,11 @@ def test_quant_config4_full_shape(cuda, qrc, oracle):
             ctx.mode = mode
             q2, s2, _ = ctx.amax_quant_e4m3(x)
             assert np.float32(s2.item()) == so and torch.equal(q, q2)
+        ctx.mode = 0
+        ctx.set_launch(1, 256)
+        ctx.set_pipeline(6)              # amax pass through the bulk-copy ring
+        q3, s3, _ = ctx.amax_quant_e4m3(x)
+        assert np.float32(s3.item()) == so and torch.equal(q, q3)
 
 
 @pytest.mark.slow
