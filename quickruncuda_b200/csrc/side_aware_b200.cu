@@ -93,7 +93,24 @@ constexpr int kMaxSm = 256;
 #ifndef QRC_LOAD_KIND
 #define QRC_LOAD_KIND 1
 #endif
+//   QRC_STEAL      1: a warp whose side queue is empty continues on the other
+//                  side's queue (far reads, only in the tail), so a die with
+//                  fewer SMs does not leave the other one idle at the end
+#ifndef QRC_STEAL
+#define QRC_STEAL 1
+#endif
+//   QRC_STRIDE_LOG2  queue positions map to pairs through an interleave: a
+//                  grab of QRC_MAX_GRAB positions covers pairs 2^this apart,
+//                  and consecutive grabs (other warps) cover adjacent pairs,
+//                  so all warps of a side work inside one compact window of
+//                  memory at a time; 0 maps positions to pairs in order
+#ifndef QRC_STRIDE_LOG2
+#define QRC_STRIDE_LOG2 11
+#endif
 constexpr qrc_u32 kMaxGrab = QRC_MAX_GRAB;
+constexpr int kStrideLog2 = QRC_STRIDE_LOG2;
+static_assert((QRC_MAX_GRAB & (QRC_MAX_GRAB - 1)) == 0, "QRC_MAX_GRAB must be a power of two");
+constexpr int kGrabLog2 = QRC_MAX_GRAB >= 16 ? 4 : QRC_MAX_GRAB >= 8 ? 3 : QRC_MAX_GRAB >= 4 ? 2 : QRC_MAX_GRAB >= 2 ? 1 : 0;
 constexpr int kVerifyRandom = 64;
 constexpr int kVerifyCal = 8;                    // anchor + partner re-probes in verification
 constexpr int kCalProbes = 16;                   // per side, calibration wave
@@ -598,11 +615,13 @@ QRC_DEV void finish_block(qrc_u32 bits, qrc_u32* map, float* out, float* scale_o
 // broadcasts lane 0's atomics).
 struct SideWalk {
     qrc_u64 lo, hi, C, mask, page_base, npairs, p, p1, nstart;
+    qrc_u64 main_pairs, tail_stride;   // interleave: full blocks, stride of the last block
     const qrc_u32* page_bits;
     qrc_u32* queue;
+    qrc_u32* other;
     qrc_u32 nsize, spread;
     int side, use_page_bits, flip;
-    bool pending;
+    bool pending, stealing;
 
     QRC_MEMBER void setup(qrc_u64 a, qrc_u64 end, qrc_u32* map, qrc_u32 mode) {
         const qrc_u64 mb = map_base(map), mbytes = map_bytes(map);
@@ -617,18 +636,24 @@ struct SideWalk {
         const qrc_u32 lab = (aware && sm < (qrc_u32)kMaxSm) ? map[O_SM_SIDE + sm] : 0u;
         side = lab ? (int)(lab - 1) : (int)(blockIdx.x & 1);
         queue = &map[side ? H_QUEUE1 : H_QUEUE0];
+        other = &map[side ? H_QUEUE0 : H_QUEUE1];
+        stealing = false;
         const qrc_u64 PAIR = 2 * C;
         lo = (a + PAIR - 1) & ~(PAIR - 1);
         hi = end & ~(PAIR - 1);
         if (hi <= lo) { lo = end; hi = end; }
         npairs = (hi - lo) / PAIR;
         spread = gridDim.x * (blockDim.x >> 5);     // ~2x the warps reading one side
+        const int block_log2 = kStrideLog2 ? kStrideLog2 + kGrabLog2 : 0;
+        main_pairs = kStrideLog2 ? (npairs >> block_log2) << block_log2 : 0;
+        tail_stride = kStrideLog2 ? (npairs - main_pairs) >> kGrabLog2 : 0;
         p = p1 = nstart = 0;
         nsize = 0;
         pending = false;
     }
     // Grab size when `seen` pairs of this side are already taken.
     QRC_MEMBER qrc_u32 grab_size(qrc_u64 seen) const {
+        if (stealing) return 1u;                 // the other side is in its tail
         const qrc_u64 left = npairs > seen ? npairs - seen : 0;
         const qrc_u64 s = left / spread;
         return s >= kMaxGrab ? kMaxGrab : (s < 1 ? 1u : (qrc_u32)s);
@@ -657,14 +682,43 @@ struct SideWalk {
         st = __shfl_sync(0xFFFFFFFFu, st, 0);
         adopt(lane, st, sz);
     }
+    // Pair index of queue position c: a bijection of [0, npairs).  Inside a
+    // block of 2^(stride+grab) positions, position r goes to pair
+    // (r mod grab) * 2^stride + r / grab; the last, partial block uses the
+    // stride that fits it; positions past that map to themselves.
+    QRC_MEMBER qrc_u64 pair_of(qrc_u64 c) const {
+        if (kStrideLog2 == 0) return c;
+        const qrc_u64 G1 = (1ull << kGrabLog2) - 1;
+        if (c < main_pairs) {
+            const int block_log2 = kStrideLog2 + kGrabLog2;
+            const qrc_u64 r = c & ((1ull << block_log2) - 1);
+            return (c - r) + ((r & G1) << kStrideLog2) + (r >> kGrabLog2);
+        }
+        const qrc_u64 r = c - main_pairs;
+        if (r < (tail_stride << kGrabLog2)) return main_pairs + (r & G1) * tail_stride + (r >> kGrabLog2);
+        return c;
+    }
     QRC_MEMBER qrc_u64 next(int lane) {
         if (p >= p1) {
             if (!pending) return 0;
             const qrc_u64 st = __shfl_sync(0xFFFFFFFFu, nstart, 0);
             const qrc_u32 sz = __shfl_sync(0xFFFFFFFFu, nsize, 0);
-            if (!adopt(lane, st, sz)) return 0;
+            if (!adopt(lane, st, sz)) {
+#if QRC_STEAL
+                if (stealing) return 0;
+                // Own side done: help the other side finish (its halves are
+                // homed on the other die, so these reads cross it).
+                stealing = true;
+                side ^= 1;
+                queue = other;
+                begin(lane);
+                if (p >= p1) return 0;
+#else
+                return 0;
+#endif
+            }
         }
-        const qrc_u64 pa = lo + p * (2 * C);
+        const qrc_u64 pa = lo + pair_of(p) * (2 * C);
         p++;
         int pbit = 0;
         if (use_page_bits) {
