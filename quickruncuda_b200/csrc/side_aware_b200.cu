@@ -107,6 +107,13 @@ constexpr int kMaxSm = 256;
 #ifndef QRC_STRIDE_LOG2
 #define QRC_STRIDE_LOG2 11
 #endif
+#ifndef QRC_TIMELINE
+#define QRC_TIMELINE 0
+#endif
+//   QRC_TIMELINE   1: each CTA of a reduction records its start and end
+//                  %globaltimer, side, SM and the chunks it read from the other
+//                  side's queue in the map (words O_TIMELINE + 4*CTA, up to
+//                  256 CTAs), for diagnostics; off by default
 constexpr qrc_u32 kMaxGrab = QRC_MAX_GRAB;
 constexpr int kStrideLog2 = QRC_STRIDE_LOG2;
 static_assert((QRC_MAX_GRAB & (QRC_MAX_GRAB - 1)) == 0, "QRC_MAX_GRAB must be a power of two");
@@ -131,6 +138,7 @@ enum : qrc_u32 {
     O_SM_SIDE = 256,                               // per SM: 0 unknown, 1 side 0, 2 side 1
     O_SM_LAT = 512,                                // per SM raw anchor latency (cycles)
     O_PAGE_LAT = 1024,                             // first kDiagPages raw page latencies
+    O_TIMELINE = 3072,                             // QRC_TIMELINE: 4 words per CTA, 256 CTAs
     O_PAGE_BITS = 4096,                            // one bit per 2 MiB page
 };
 
@@ -622,6 +630,7 @@ struct SideWalk {
     qrc_u32 nsize, spread;
     int side, use_page_bits, flip;
     bool pending, stealing;
+    qrc_u32 stolen;                    // chunks read through the other side's queue
 
     QRC_MEMBER void setup(qrc_u64 a, qrc_u64 end, qrc_u32* map, qrc_u32 mode) {
         const qrc_u64 mb = map_base(map), mbytes = map_bytes(map);
@@ -638,6 +647,7 @@ struct SideWalk {
         queue = &map[side ? H_QUEUE1 : H_QUEUE0];
         other = &map[side ? H_QUEUE0 : H_QUEUE1];
         stealing = false;
+        stolen = 0;
         const qrc_u64 PAIR = 2 * C;
         lo = (a + PAIR - 1) & ~(PAIR - 1);
         hi = end & ~(PAIR - 1);
@@ -720,6 +730,7 @@ struct SideWalk {
         }
         const qrc_u64 pa = lo + pair_of(p) * (2 * C);
         p++;
+        stolen += stealing ? 1u : 0u;
         int pbit = 0;
         if (use_page_bits) {
             const qrc_u64 pg = (pa - page_base) >> 21;
@@ -885,6 +896,10 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, float* out, floa
         SideWalk w;
         w.setup(a, end, map, mode);
         lo = w.lo; hi = w.hi;
+#if QRC_TIMELINE
+        qrc_u64 t_start;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_start));
+#endif
         const int S = bulk_slots_per_warp(dynamic_smem_size(), W);
 #ifndef QRC_CHECKED
         if (S >= 2) {
@@ -897,6 +912,22 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, float* out, floa
             for (qrc_u64 chunk = w.next(lane); chunk; chunk = w.next(lane))
                 acc = chunk_warp<Op>(acc, chunk, n512, lane QRC_CS_ARG);
         }
+#if QRC_TIMELINE
+        {
+            __shared__ qrc_u32 s_stolen;
+            if (threadIdx.x == 0) s_stolen = 0;
+            __syncthreads();
+            if (lane == 0 && w.stolen) atomicAdd(&s_stolen, w.stolen);
+            __syncthreads();
+            qrc_u64 t_end;
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_end));
+            if (threadIdx.x == 0 && blockIdx.x < 256) {
+                qrc_u32* tl = map + O_TIMELINE + 4 * blockIdx.x;
+                tl[0] = (qrc_u32)t_start; tl[1] = (qrc_u32)t_end;
+                tl[2] = (qrc_u32)w.side | (s_stolen << 1); tl[3] = smid();
+            }
+        }
+#endif
     }
     // Edges shorter than the body granule: head by CTA 0 warp 0, tail by the
     // last CTA's last warp.
