@@ -131,6 +131,26 @@ int qrc_ctx_set_pipeline(qrc_ctx* ctx, int bulk_slots_per_warp);
  * tests/side_aware.cu:257-395) with C[0] as the output. */
 int qrc_absmax_f32(const float* d_in, size_t n, float* d_out, qrc_ctx* ctx, void* stream);
 
+/* Same reduction for callers that cannot allocate device memory: a host
+ * application that reserves all device memory up front and hands this code
+ * only the buffers it works on, a process held to a fixed memory budget, or
+ * code that must avoid the implicit synchronisation cudaMalloc may cause.
+ * Neither this call nor anything it calls allocates: no context is needed,
+ * and its scratch (side map, work queues, ticket, accumulator; 20 KiB) is a
+ * fixed array that every GPU loading this library holds until exit.  Runs on
+ * the current device, asynchronously on `stream`.
+ *   - Limit: the input may span at most 32768 pages of 2 MiB (64 GiB, about
+ *     16e9 floats); larger inputs return QRC_ERR_RANGE before any GPU work.
+ *   - The first call on a device looks up the array's device address
+ *     (cudaGetSymbolAddress); make it before any stream capture.
+ *   - The array remembers the last input range: a call on a new range clears
+ *     it and runs side discovery for that range first (about 1-2 ms for 4 GB);
+ *     repeated calls on the same buffer reuse the map.
+ *   - Every call on a device shares the one array, so calls that overlap on
+ *     the GPU (other streams, other host threads) race; serialise them.
+ * Result and errors as qrc_absmax_f32.  No counterpart in the reference. */
+int qrc_absmax_f32_noalloc(const float* d_in, size_t n, float* d_out, void* stream);
+
 /* Same result from a host buffer: copies h_in to a device staging buffer owned
  * by the context (allocated and side-mapped on first use, regrown when n grows),
  * reduces it and copies the result to *h_out.  Synchronous.  Pinned host memory

@@ -59,6 +59,7 @@ SIGNATURES = [
     ("qrc_ctx_set_launch", c_int, [c_void_p, c_int, c_int]),
     ("qrc_ctx_set_pipeline", c_int, [c_void_p, c_int]),
     ("qrc_absmax_f32", c_int, [c_void_p, c_size, c_void_p, c_void_p, c_void_p]),
+    ("qrc_absmax_f32_noalloc", c_int, [c_void_p, c_size, c_void_p, c_void_p]),
     ("qrc_absmax_f32_host", c_int, [c_void_p, c_size, ctypes.POINTER(c_float), c_void_p, c_void_p]),
     ("qrc_amax_quant_e4m3", c_int, [c_void_p, c_size, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
     ("qrc_fill_uniform_f32", c_int, [c_void_p, c_size, c_u64, c_u64, c_void_p]),

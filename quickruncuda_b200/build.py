@@ -29,7 +29,7 @@ GENCODE = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_COMMON = GENCODE + ["-lineinfo", "-O3", "--std=c++17", "-Xptxas", "-v",
                          "-Xcompiler", "-fPIC,-fopenmp,-fvisibility=hidden"]
 
-LIB_SOURCES = [CSRC / "qrc_abi.cu", CSRC / "side_aware_b200.cu", CSRC / "qrc_gen.cuh",
+LIB_SOURCES = [CSRC / "qrc_abi.cu", CSRC / "qrc_noalloc.cu", CSRC / "side_aware_b200.cu", CSRC / "qrc_gen.cuh",
                INCLUDE / "qrc_b200.h", INCLUDE / "qrc_b200_debug.h"]
 HARNESS_SOURCES = [PKG / "harness" / "qrc_harness.cpp", CSRC / "qrc_gen.cuh"]
 
@@ -64,7 +64,8 @@ def build_lib(checked: bool = False, force: bool = False, verbose: bool = False)
         return out
     LIB_DIR.mkdir(parents=True, exist_ok=True)
     tmp = out.with_suffix(".so.tmp")
-    cmd = [NVCC, *NVCC_COMMON, "-shared", "-o", str(tmp), str(CSRC / "qrc_abi.cu"), "-lgomp"]
+    cmd = [NVCC, *NVCC_COMMON, "-shared", "-o", str(tmp), str(CSRC / "qrc_abi.cu"), str(CSRC / "qrc_noalloc.cu"),
+           "-lgomp"]
     if checked:
         cmd.insert(1, "-DQRC_CHECKED")
     _run(cmd, log=LIB_DIR / (out.name + ".buildlog"), verbose=verbose)
