@@ -123,6 +123,15 @@ int qrc_ctx_set_launch(qrc_ctx* ctx, int blocks_per_sm, int threads_per_block);
  * tests/side_aware.cu:319-325). */
 int qrc_ctx_set_pipeline(qrc_ctx* ctx, int bulk_slots_per_warp);
 
+/* Programmatic dependent launch of reductions (1, the default) or plain
+ * stream order (0).  With 1, a reduction's CTAs may be scheduled while the
+ * previous kernel in the stream drains; each reduction still waits for that
+ * kernel to complete before it uses any memory (griddepcontrol.wait), so
+ * results and ordering are unchanged and only launch latency is hidden.
+ * No reference counterpart (the harness launches with cuLaunchKernel,
+ * QuickRunCUDA.cpp:528-532). */
+int qrc_ctx_set_overlap(qrc_ctx* ctx, int enable);
+
 /* *d_out = max_i |d_in[i]| over n floats (IEEE maxNum: NaN inputs are ignored,
  * -0 gives +0, n == 0 gives +0).  d_in must be 4-byte aligned; the side-aware
  * path applies when [d_in, d_in + n) lies inside the context's buffer.

@@ -58,6 +58,7 @@ SIGNATURES = [
     ("qrc_ctx_set_mode", c_int, [c_void_p, c_int]),
     ("qrc_ctx_set_launch", c_int, [c_void_p, c_int, c_int]),
     ("qrc_ctx_set_pipeline", c_int, [c_void_p, c_int]),
+    ("qrc_ctx_set_overlap", c_int, [c_void_p, c_int]),
     ("qrc_absmax_f32", c_int, [c_void_p, c_size, c_void_p, c_void_p, c_void_p]),
     ("qrc_absmax_f32_noalloc", c_int, [c_void_p, c_size, c_void_p, c_void_p]),
     ("qrc_absmax_f32_host", c_int, [c_void_p, c_size, ctypes.POINTER(c_float), c_void_p, c_void_p]),

@@ -125,6 +125,10 @@ class SideAwareContext:
         nat.check(self.lib, "qrc_ctx_set_pipeline",
                   self.lib.qrc_ctx_set_pipeline(self.handle, bulk_slots_per_warp))
 
+    def set_overlap(self, enable: bool) -> None:
+        """Programmatic dependent launch of reductions (hides launch latency)."""
+        nat.check(self.lib, "qrc_ctx_set_overlap", self.lib.qrc_ctx_set_overlap(self.handle, int(bool(enable))))
+
     # -- work --------------------------------------------------------------
     def absmax(self, x, out=None, n: Optional[int] = None, stream=None):
         """max |x| of a float32 CUDA tensor (or raw pointer + n) into `out`

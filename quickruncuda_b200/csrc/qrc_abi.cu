@@ -149,6 +149,7 @@ struct qrc_ctx {
     int blocks_per_sm = 1;
     int threads = 1024;
     int bulk_slots = 0;             // 0: register loads; >= 2: bulk-copy staging slots per warp
+    int overlap = 1;                // programmatic dependent launch of reductions
     const void* base = nullptr;
     size_t bytes = 0;
     qrc_u32* d_map = nullptr;
@@ -200,16 +201,36 @@ static cudaError_t allow_smem(size_t smem) {
     return cudaSuccess;
 }
 
+// Launches `kernel` with programmatic stream serialization when the context
+// allows overlap: the kernel's CTAs may then be scheduled while the previous
+// grid in the stream drains; the kernel itself waits (griddepcontrol.wait)
+// before it touches anything the previous grid could still be using.
+template <typename... KArgs, typename... Args>
+static cudaError_t launch(const qrc_ctx* c, void (*kernel)(KArgs...), int grid, int block, size_t smem,
+                          cudaStream_t s, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(block);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = c->overlap ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 static int launch_absmax(qrc_ctx* c, const float* in, size_t n, float* out, cudaStream_t s) {
     const int grid = c->num_sms * c->blocks_per_sm;
     const qrc_u32 mode = (qrc_u32)c->mode;
     const size_t smem = launch_smem(c);
+    const qrc_u64 n64 = n;
     switch (c->threads) {
-        case 1024: QRC_CK(allow_smem<1024>(smem)); qrc_k_absmax_f32<1024><<<grid, 1024, smem, s>>>(in, n, c->d_map, out, mode); break;
-        case 512:  QRC_CK(allow_smem<512>(smem)); qrc_k_absmax_f32<512><<<grid, 512, smem, s>>>(in, n, c->d_map, out, mode); break;
-        default:   QRC_CK(allow_smem<256>(smem)); qrc_k_absmax_f32<256><<<grid, 256, smem, s>>>(in, n, c->d_map, out, mode); break;
+        case 1024: QRC_CK(allow_smem<1024>(smem)); QRC_CK(launch(c, qrc_k_absmax_f32<1024>, grid, 1024, smem, s, in, n64, c->d_map, out, mode)); break;
+        case 512:  QRC_CK(allow_smem<512>(smem)); QRC_CK(launch(c, qrc_k_absmax_f32<512>, grid, 512, smem, s, in, n64, c->d_map, out, mode)); break;
+        default:   QRC_CK(allow_smem<256>(smem)); QRC_CK(launch(c, qrc_k_absmax_f32<256>, grid, 256, smem, s, in, n64, c->d_map, out, mode)); break;
     }
-    QRC_CK(cudaGetLastError());
     return QRC_OK;
 }
 
@@ -309,6 +330,13 @@ QRC_API int qrc_ctx_set_pipeline(qrc_ctx* c, int slots) {
     return QRC_OK;
 }
 
+QRC_API int qrc_ctx_set_overlap(qrc_ctx* c, int enable) {
+    if (!c || (enable != 0 && enable != 1)) return QRC_ERR_INVALID;
+    c->overlap = enable;
+    if (c->stage_ctx) c->stage_ctx->overlap = enable;
+    return QRC_OK;
+}
+
 QRC_API int qrc_absmax_f32(const float* d_in, size_t n, float* d_out, qrc_ctx* c, void* stream) {
     if (!c || !d_out || (n && !d_in) || ((uintptr_t)d_in & 3)) return QRC_ERR_INVALID;
     if (n > ((size_t)1 << 61)) return QRC_ERR_RANGE;
@@ -333,6 +361,7 @@ QRC_API int qrc_absmax_f32_host(const float* h_in, size_t n, float* h_out, qrc_c
         c->stage_ctx->blocks_per_sm = c->blocks_per_sm;
         c->stage_ctx->threads = c->threads;
         c->stage_ctx->bulk_slots = c->bulk_slots;
+        c->stage_ctx->overlap = c->overlap;
     }
     qrc_ctx* sc = c->stage_ctx ? c->stage_ctx : c;
     if (n) QRC_CK(cudaMemcpyAsync(c->d_stage, h_in, n * sizeof(float), cudaMemcpyHostToDevice, s));

@@ -157,6 +157,12 @@ QRC_DEV qrc_u32 smid() {
 
 QRC_DEV int parity64(qrc_u64 x) { return __popcll(x) & 1; }
 
+// Programmatic dependent launch: wait for the preceding grid in the stream to
+// complete (and its memory to be visible); allow the next grid to be scheduled
+// while this one drains.  Both are no-ops unless the launch opted in.
+QRC_DEV void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+QRC_DEV void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // Cycles for kProbeIters dependent L2 atomics on `w`.  atomicCAS(w, v, v) with v
 // the current value writes back the value it found, so memory never changes,
 // and each CAS needs the previous result as its compare operand.  The first
@@ -606,6 +612,11 @@ QRC_DEV void finish_block(qrc_u32 bits, qrc_u32* map, float* out, float* scale_o
                 map[H_QUEUE1] = 0u;
                 if (map[H_WAIT_ERR]) r = 0x7FFFFFFFu;   // a bounded wait gave up: no valid maximum
                 out[0] = __uint_as_float(r);
+#if QRC_TIMELINE
+                qrc_u64 t_fin;
+                asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_fin));
+                map[O_TIMELINE + 1023] = (qrc_u32)t_fin;      // end of the launch's last CTA
+#endif
                 if (scale_out) scale_out[0] = e4m3_scale_from_amax(__uint_as_float(r));
             }
         }
@@ -876,6 +887,7 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, float* out, floa
 
     if (mode == MODE_STREAM) {
         // Side-agnostic grid-stride stream over the 16-byte aligned body.
+        griddep_wait();
         lo = (a + 15) & ~15ull; hi = end & ~15ull;
         if (hi <= lo) { lo = end; hi = end; }
         const qrc_u64 nv = (hi - lo) / 16;
@@ -892,10 +904,12 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, float* out, floa
             #pragma unroll
             for (int u = 0; u < 8; u++) acc = Op::step16(acc, v[u]);
         }
+        griddep_launch_dependents();
     } else {
         SideWalk w;
-        w.setup(a, end, map, mode);
+        w.setup(a, end, map, mode);       // reads only the map header, which reductions never write
         lo = w.lo; hi = w.hi;
+        griddep_wait();                   // the queues and accumulator of the previous launch are reset
 #if QRC_TIMELINE
         qrc_u64 t_start;
         asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_start));
@@ -912,6 +926,7 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, float* out, floa
             for (qrc_u64 chunk = w.next(lane); chunk; chunk = w.next(lane))
                 acc = chunk_warp<Op>(acc, chunk, n512, lane QRC_CS_ARG);
         }
+        griddep_launch_dependents();
 #if QRC_TIMELINE
         {
             __shared__ qrc_u32 s_stolen;

@@ -180,12 +180,16 @@ def test_absmax_signalling_nan_and_random_bits(cuda, qrc, oracle):
             assert _bits(ctx.absmax(x)) == oracle.absmax_bits(u.view(np.float32))
 
 
-def test_back_to_back_launches_reset_scratch(buf, oracle):
+@pytest.mark.parametrize("overlap", [1, 0])
+def test_back_to_back_launches_reset_scratch(buf, oracle, overlap):
     """Each launch leaves queues, ticket and accumulator at zero, so results
     of consecutive launches on different data are independent (the reference
-    relied on stale scratch, tests/side_aware.cu:371-374)."""
+    relied on stale scratch, tests/side_aware.cu:371-374).  With programmatic
+    dependent launch (overlap=1) each launch still sees the previous one's
+    reset and the tensor writes between launches."""
     import torch
     x, ctx = buf
+    ctx.set_overlap(overlap)
     n = 4 * MIB
     view = x[:n]
     saved = view.clone()
@@ -198,6 +202,7 @@ def test_back_to_back_launches_reset_scratch(buf, oracle):
         assert outs.cpu().tolist() == [float(100 - i) for i in range(64)]
     finally:
         view.copy_(saved)
+        ctx.set_overlap(1)
 
 
 def test_context_without_map_and_foreign_range(cuda, qrc, oracle):
