@@ -110,6 +110,11 @@ constexpr int kMaxSm = 256;
 #ifndef QRC_TIMELINE
 #define QRC_TIMELINE 0
 #endif
+//   QRC_FINISH     1: block maxima leave as red.max and one acquire-release
+//                  ticket atomic; 0: atomicMax, fence, ticket, fence
+#ifndef QRC_FINISH
+#define QRC_FINISH 1
+#endif
 //   QRC_TIMELINE   1: each CTA of a reduction records its start and end
 //                  %globaltimer, side, SM and the chunks it read from the other
 //                  side's queue in the map (words O_TIMELINE + 4*CTA, up to
@@ -602,11 +607,23 @@ QRC_DEV void finish_block(qrc_u32 bits, qrc_u32* map, float* out, float* scale_o
         qrc_u32 v = lane < W ? s_w[lane] : 0u;
         v = __reduce_max_sync(0xFFFFFFFFu, v);
         if (lane == 0) {
+#if QRC_FINISH == 1
+            // The block's maximum goes out as a fire-and-forget reduction;
+            // the ticket increment has release semantics (it is ordered after
+            // that reduction) and acquire semantics (the last CTA then sees
+            // every other CTA's reduction).
+            qrc_u32 t;
+            asm volatile("red.relaxed.gpu.global.max.u32 [%0], %1;" :: "l"(&map[H_ACC]), "r"(v) : "memory");
+            asm volatile("atom.acq_rel.gpu.global.inc.u32 %0, [%1], %2;"
+                         : "=r"(t) : "l"(&map[H_RUN_TICKET]), "r"(gridDim.x - 1) : "memory");
+            if (t == gridDim.x - 1) {
+#else
             atomicMax(&map[H_ACC], v);
             __threadfence();
             const qrc_u32 t = atomicInc(&map[H_RUN_TICKET], gridDim.x - 1);
             if (t == gridDim.x - 1) {
                 __threadfence();
+#endif
                 qrc_u32 r = atomicExch(&map[H_ACC], 0u);
                 map[H_QUEUE0] = 0u;
                 map[H_QUEUE1] = 0u;
