@@ -51,6 +51,7 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-ablation", action="store_true")
+    ap.add_argument("--no-quant", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=0, help="0 = min(10, max(3, steps // 100))")
     ap.add_argument("--n-per-gpu", type=int, default=N_PER_GPU,
                     help="floats per GPU (default 1e9; smaller sizes are for profiling captures)")
@@ -62,6 +63,15 @@ def dist_env():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", str(rank)))
     return rank, world, local
+
+
+def host_threads() -> int:
+    """All host cores this process may run on (torchrun sets OMP_NUM_THREADS=1
+    for its workers; the CPU baseline must not inherit that)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:  # pragma: no cover
+        return os.cpu_count() or 1
 
 
 def measured_peak():
@@ -162,12 +172,13 @@ def run_reference(args):
     x = orc.uniform_with_outlier(1, n, OUTLIER)
     used = ctypes.c_int()
     fptr = x.ctypes.data_as(ctypes.POINTER(ctypes.c_float))
+    nthr = host_threads()
     for _ in range(max(args.warmup, 1)):
-        orc.lib.oracle_absmax_f32(fptr, n, 0, ctypes.byref(used))
+        orc.lib.oracle_absmax_f32(fptr, n, nthr, ctypes.byref(used))
     times = []
     for _ in range(args.steps):
         t0 = time.perf_counter()
-        r = orc.lib.oracle_absmax_f32(fptr, n, 0, ctypes.byref(used))
+        r = orc.lib.oracle_absmax_f32(fptr, n, nthr, ctypes.byref(used))
         times.append(time.perf_counter() - t0)
     assert r == OUTLIER, r
     total = sum(times)
@@ -284,6 +295,34 @@ def run_ours(args):
             ablation[m] = round(nbytes / (s.elapsed_time(e) / abl_steps / 1e3) / 1e9, 2)
         ctx.mode = args.mode
 
+    # ---- fused amax -> e4m3 quantize, bf16 [16384, 8192] normal(0, 2) seed 3 ----
+    quant = None
+    if not args.no_quant and world == 1:
+        nq = 16384 * 8192
+        xq = torch.empty(nq, dtype=torch.int16, device=dev)
+        q.fill_normal_bf16(xq, seed=3, sigma=2.0)
+        qout = torch.empty(nq, dtype=torch.uint8, device=dev)
+        qscale = torch.empty(1, dtype=torch.float32, device=dev)
+        qamax = torch.empty(1, dtype=torch.float32, device=dev)
+        with q.SideAwareContext(xq, device=local) as cq:
+            for _ in range(3):
+                cq.amax_quant_e4m3(xq, q=qout, scale=qscale, amax=qamax)
+            qsteps = max(3, min(args.steps, 300))
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record(stream)
+            for _ in range(qsteps):
+                cq.amax_quant_e4m3(xq, q=qout, scale=qscale, amax=qamax)
+            e.record(stream)
+            torch.cuda.synchronize()
+        qms = s.elapsed_time(e) / qsteps
+        qbytes = 2 * 2 * nq + nq          # two reads of the bf16 input (amax, then quantize) + one e4m3 write
+        qgbs = qbytes / (qms / 1e3) / 1e9
+        peak, _ = measured_peak()
+        quant = {"workload": "bf16 [16384, 8192] normal(0,2) seed 3 -> e4m3 + scale", "ms": round(qms, 5),
+                 "gbs": round(qgbs, 2), "algorithmic_bytes": qbytes, "launches_per_step": 2,
+                 "roofline_frac": round(qgbs / peak, 4), "scale": float(qscale.item()), "amax": float(qamax.item())}
+        del xq, qout
+
     # ---- end to end through the host-buffer C-ABI call ----
     e2e = None
     h_ptr = None
@@ -338,14 +377,15 @@ def run_ours(args):
             h_ptr[gi] = OUTLIER * sign
         fptr = ctypes.cast(ctypes.c_void_p(h_ptr.data_ptr()), ctypes.POINTER(ctypes.c_float))
         used = ctypes.c_int()
+        nthr = host_threads()
         t0 = time.perf_counter()
-        r = orc.lib.oracle_absmax_f32(fptr, n, 0, ctypes.byref(used))
+        r = orc.lib.oracle_absmax_f32(fptr, n, nthr, ctypes.byref(used))
         t1 = time.perf_counter() - t0
         reps = int(min(10, max(3, 10.0 // max(t1, 1e-3))))
         ts = []
         for _ in range(reps):
             t0 = time.perf_counter()
-            r = orc.lib.oracle_absmax_f32(fptr, n, 0, ctypes.byref(used))
+            r = orc.lib.oracle_absmax_f32(fptr, n, nthr, ctypes.byref(used))
             ts.append(time.perf_counter() - t0)
         assert r == OUTLIER
         med = statistics.median(ts)
@@ -377,6 +417,7 @@ def run_ours(args):
                                           "num_pages", "verify_probes", "verify_mismatches")},
         "init_ms": round(init_ms, 2),
         "ablation_gbs": ablation or None,
+        "quant_e4m3": quant,
     }
     if world > 1:
         line["per_gpu_gbs"] = round(achieved, 2)
@@ -391,6 +432,13 @@ def run_ours(args):
 
 def main():
     args = parse_args()
+    # Host-side OpenMP (data generation, CPU baselines): torchrun sets
+    # OMP_NUM_THREADS=1 for its workers.  The reference arm runs alone on rank
+    # 0 and takes every core; our ranks share the cores.  Set before any
+    # OpenMP runtime is loaded.
+    _, world, _ = dist_env()
+    os.environ["OMP_NUM_THREADS"] = str(host_threads() if args.impl == "reference"
+                                        else max(1, host_threads() // world))
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)

@@ -55,10 +55,14 @@ static __device__ __forceinline__ unsigned short quant_word(qrc_u32 w, float s) 
 }
 
 // Quantize pass: 8 bf16 (16 B) in -> 8 e4m3 (8 B) out per unit, four units in
-// flight per thread.  Vector path needs in % 16 == 0 and q % 8 == 0; any other
-// alignment takes the element path.
+// flight per thread.  Units are walked from the top of the buffer down: the
+// amax pass just before ended at the top, so the first ~100 MB this pass reads
+// are still in the 126 MB L2.  Output stores are streaming (evict-first).
+// Vector path needs in % 16 == 0 and q % 8 == 0; any other alignment takes the
+// element path.
 __global__ void __launch_bounds__(512, 2)
 qrc_k_quant_e4m3(const uint16_t* in, qrc_u64 n, uint8_t* q, const float* scale_p) {
+    qrc::griddep_wait();                     // the scale comes from the amax launch before
     const float s = *scale_p;
     const qrc_u64 tid = (qrc_u64)blockIdx.x * blockDim.x + threadIdx.x;
     const qrc_u64 stride = (qrc_u64)gridDim.x * blockDim.x;
@@ -69,7 +73,7 @@ qrc_k_quant_e4m3(const uint16_t* in, qrc_u64 n, uint8_t* q, const float* scale_p
         #pragma unroll
         for (int u = 0; u < 4; u++) {
             const qrc_u64 j = i + u * stride;
-            if (j < nv) v[u] = qrc::ld_stream16((qrc_u64)(in + 8 * j));
+            if (j < nv) v[u] = qrc::ld_stream16((qrc_u64)(in + 8 * (nv - 1 - j)));
         }
         #pragma unroll
         for (int u = 0; u < 4; u++) {
@@ -78,7 +82,7 @@ qrc_k_quant_e4m3(const uint16_t* in, qrc_u64 n, uint8_t* q, const float* scale_p
                 uint2 o;
                 o.x = (qrc_u32)quant_word(v[u].x, s) | ((qrc_u32)quant_word(v[u].y, s) << 16);
                 o.y = (qrc_u32)quant_word(v[u].z, s) | ((qrc_u32)quant_word(v[u].w, s) << 16);
-                __stcs((uint2*)(q + 8 * j), o);
+                __stcs((uint2*)(q + 8 * (nv - 1 - j)), o);
             }
         }
     }
@@ -381,16 +385,14 @@ QRC_API int qrc_amax_quant_e4m3(const uint16_t* d_in, size_t n, uint8_t* d_q, fl
     float* amax = d_amax ? d_amax : c->d_scalars;
     const int grid = c->num_sms * c->blocks_per_sm;
     const size_t smem = launch_smem(c);
+    const qrc_u64 n64 = n;
+    const qrc_u32 mode = (qrc_u32)c->mode;
     switch (c->threads) {
-        case 1024: QRC_CK(allow_smem<1024>(smem)); qrc_k_amax_bf16<1024><<<grid, 1024, smem, s>>>(d_in, n, c->d_map, amax, d_scale, c->mode); break;
-        case 512:  QRC_CK(allow_smem<512>(smem)); qrc_k_amax_bf16<512><<<grid, 512, smem, s>>>(d_in, n, c->d_map, amax, d_scale, c->mode); break;
-        default:   QRC_CK(allow_smem<256>(smem)); qrc_k_amax_bf16<256><<<grid, 256, smem, s>>>(d_in, n, c->d_map, amax, d_scale, c->mode); break;
+        case 1024: QRC_CK(allow_smem<1024>(smem)); QRC_CK(launch(c, qrc_k_amax_bf16<1024>, grid, 1024, smem, s, d_in, n64, c->d_map, amax, d_scale, mode)); break;
+        case 512:  QRC_CK(allow_smem<512>(smem)); QRC_CK(launch(c, qrc_k_amax_bf16<512>, grid, 512, smem, s, d_in, n64, c->d_map, amax, d_scale, mode)); break;
+        default:   QRC_CK(allow_smem<256>(smem)); QRC_CK(launch(c, qrc_k_amax_bf16<256>, grid, 256, smem, s, d_in, n64, c->d_map, amax, d_scale, mode)); break;
     }
-    QRC_CK(cudaGetLastError());
-    if (n) {
-        qrc_k_quant_e4m3<<<c->num_sms * 2, 512, 0, s>>>(d_in, n, d_q, d_scale);
-        QRC_CK(cudaGetLastError());
-    }
+    if (n) QRC_CK(launch(c, qrc_k_quant_e4m3, c->num_sms * 2, 512, 0, s, d_in, n64, d_q, (const float*)d_scale));
     return QRC_OK;
 }
 
