@@ -52,6 +52,8 @@ def parse_args():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-ablation", action="store_true")
     ap.add_argument("--no-quant", action="store_true")
+    ap.add_argument("--no-overlap", action="store_true",
+                    help="launch reductions in plain stream order (no programmatic dependent launch)")
     ap.add_argument("--e2e-steps", type=int, default=0, help="0 = min(10, max(3, steps // 100))")
     ap.add_argument("--n-per-gpu", type=int, default=N_PER_GPU,
                     help="floats per GPU (default 1e9; smaller sizes are for profiling captures)")
@@ -242,6 +244,7 @@ def run_ours(args):
     init_ms = 1e3 * (time.perf_counter() - t0)
     info = ctx.info
     ctx.mode = args.mode
+    ctx.set_overlap(not args.no_overlap)
     out = torch.zeros(1, dtype=torch.float32, device=dev)
 
     def step():
@@ -406,6 +409,7 @@ def run_ours(args):
         "warmup": max(args.warmup, 3), "ms_per_step": round(ms_per_step, 5), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": workload, "n_per_gpu": n, "bytes_per_gpu": nbytes, "mode": args.mode,
+                   "overlap": not args.no_overlap,
                    "launch": f"{info['num_sms_measured'] or ''} SMs x 1 CTA x 1024 threads",
                    "l2": L2_NOTE, "parallelism": "replicated shards" if world == 1 else f"shard{world}+nccl_max_allreduce"},
         "roofline": roofline,
