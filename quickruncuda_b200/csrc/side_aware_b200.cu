@@ -120,7 +120,6 @@ constexpr int kMaxSm = 256;
 //                  side's queue in the map (words O_TIMELINE + 4*CTA, up to
 //                  256 CTAs), for diagnostics; off by default
 constexpr qrc_u32 kMaxGrab = QRC_MAX_GRAB;
-constexpr int kSubQueues = 4;                    // queue slices per side (separate atomic counters)
 constexpr int kStrideLog2 = QRC_STRIDE_LOG2;
 static_assert((QRC_MAX_GRAB & (QRC_MAX_GRAB - 1)) == 0, "QRC_MAX_GRAB must be a power of two");
 constexpr int kGrabLog2 = QRC_MAX_GRAB >= 16 ? 4 : QRC_MAX_GRAB >= 8 ? 3 : QRC_MAX_GRAB >= 4 ? 2 : QRC_MAX_GRAB >= 2 ? 1 : 0;
@@ -137,12 +136,12 @@ enum : qrc_u32 {
     H_VERIFY_N = 12, H_VERIFY_BAD = 13, H_LAT0 = 14, H_LAT1 = 15, H_INIT_TICKET = 16,
     H_RUN_TICKET = 17, H_ACC = 18, H_PAGE_WORDS_CAP = 19, H_MASK_MEASURED = 20,
     H_SM_C0 = 21, H_SM_C1 = 22, H_BIT_C0 = 23, H_BIT_C1 = 24, H_SMID_LAST = 25,
+    H_QUEUE0 = 32, H_QUEUE1 = 64,                  // each on its own 128-byte line
     H_ERR = 96, H_ERR_ADDR_LO = 97, H_ERR_ADDR_HI = 98, H_WAIT_ERR = 99,
     H_COV_BYTES_LO = 100, H_COV_BYTES_HI = 101, H_COV_XOR_LO = 102, H_COV_XOR_HI = 103,
     O_BITLAT = 128,                                // 21 raw latencies of the mask probes
     O_SM_SIDE = 256,                               // per SM: 0 unknown, 1 side 0, 2 side 1
     O_SM_LAT = 512,                                // per SM raw anchor latency (cycles)
-    O_QUEUES = 768,                                // 2 sides x 4 slice counters, one 128-byte line each
     O_PAGE_LAT = 1024,                             // first kDiagPages raw page latencies
     O_TIMELINE = 3072,                             // QRC_TIMELINE: 4 words per CTA, 256 CTAs
     O_PAGE_BITS = 4096,                            // one bit per 2 MiB page
@@ -626,7 +625,8 @@ QRC_DEV void finish_block(qrc_u32 bits, qrc_u32* map, float* out, float* scale_o
                 __threadfence();
 #endif
                 qrc_u32 r = atomicExch(&map[H_ACC], 0u);
-                for (int k = 0; k < 2 * kSubQueues; k++) map[O_QUEUES + 32 * k] = 0u;
+                map[H_QUEUE0] = 0u;
+                map[H_QUEUE1] = 0u;
                 if (map[H_WAIT_ERR]) r = 0x7FFFFFFFu;   // a bounded wait gave up: no valid maximum
                 out[0] = __uint_as_float(r);
 #if QRC_TIMELINE
@@ -642,39 +642,25 @@ QRC_DEV void finish_block(qrc_u32 bits, qrc_u32* map, float* out, float* scale_o
 
 // Per-warp walk over the pairs of one side.  Built from the side map (or
 // without one: mask 0, page bits 0), it hands each call the address of the
-// next C-byte chunk this warp must read.
-//
-//   * Static round: the first min(npairs, warps/2) pairs are split into
-//     chunks, chunk h going to the warp whose global index is h; a warp reads
-//     its chunk whichever die it is homed on.  No atomic is involved, so every
-//     warp starts loading at once (inputs under ~19 MB are covered entirely
-//     here), while its first queue request is already in flight.
-//   * Queues: the remaining pairs are split into kSubQueues slices; each side
-//     has one atomic counter per slice (own 128-byte line), and a warp starts
-//     on slice (warp index mod kSubQueues), moving to the next slice when one
-//     runs out.  Per slice, a warp adds its grab size and owns the positions
-//     between the old and new counter value; positions map to pairs through
-//     the interleave of pair_of().  For every pair the warp reads the half
-//     homed on its own side.
-//   * Grabs are guided: QRC_MAX_GRAB pairs while plenty are left, shrinking
-//     to one pair near the end of a slice.  The next grab is requested while
-//     the current one is read.
-//   * With QRC_STEAL, a warp whose side is done walks the other side's slices
-//     with one-pair grabs (far reads, tail only).
-// Both sides walk every pair of the queued region, one half each, and the
-// static round reads both halves of its pairs: every byte is read once
-// whatever the map says.  All lanes call next() together.
+// next C-byte chunk this warp must read.  Work comes from the side's queue, a
+// counter of pairs: a warp adds its grab size and owns the pairs between the
+// old and new value.  Grabs are guided: QRC_MAX_GRAB pairs while plenty are
+// left, shrinking to one pair as the queue empties, so all warps of a side
+// finish within about one chunk of each other.  The next grab is requested
+// while the current one is read.  All lanes call next() together (it
+// broadcasts lane 0's atomics).
 struct SideWalk {
-    qrc_u64 lo, hi, C, mask, page_base, npairs, nstatic, p, p1, nstart;
+    qrc_u64 lo, hi, C, mask, page_base, npairs, p, p1, nstart;
+    qrc_u64 main_pairs, tail_stride;   // interleave: full blocks, stride of the last block
     const qrc_u32* page_bits;
-    qrc_u32* map;
-    qrc_u32 nsize, spread, warp_id;
-    int side, qside, slice, slices_left, use_page_bits, flip;
-    bool pending, stealing, static_done;
+    qrc_u32* queue;
+    qrc_u32* other;
+    qrc_u32 nsize, spread;
+    int side, use_page_bits, flip;
+    bool pending, stealing;
     qrc_u32 stolen;                    // chunks read through the other side's queue
 
-    QRC_MEMBER void setup(qrc_u64 a, qrc_u64 end, qrc_u32* map_, qrc_u32 mode) {
-        map = map_;
+    QRC_MEMBER void setup(qrc_u64 a, qrc_u64 end, qrc_u32* map, qrc_u32 mode) {
         const qrc_u64 mb = map_base(map), mbytes = map_bytes(map);
         const bool aware = map[H_MAGIC] == kMagic && map[H_STATUS] == ST_OK && a >= mb && end <= mb + mbytes;
         mask = aware ? map[H_MASK] : 0u;
@@ -686,131 +672,91 @@ struct SideWalk {
         const qrc_u32 sm = smid();
         const qrc_u32 lab = (aware && sm < (qrc_u32)kMaxSm) ? map[O_SM_SIDE + sm] : 0u;
         side = lab ? (int)(lab - 1) : (int)(blockIdx.x & 1);
+        queue = &map[side ? H_QUEUE1 : H_QUEUE0];
+        other = &map[side ? H_QUEUE0 : H_QUEUE1];
+        stealing = false;
+        stolen = 0;
         const qrc_u64 PAIR = 2 * C;
         lo = (a + PAIR - 1) & ~(PAIR - 1);
         hi = end & ~(PAIR - 1);
         if (hi <= lo) { lo = end; hi = end; }
         npairs = (hi - lo) / PAIR;
-        spread = gridDim.x * (blockDim.x >> 5);
-        warp_id = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-        nstatic = npairs < spread / 2 ? npairs : spread / 2;
-        qside = side;
-        slice = (int)(warp_id % kSubQueues);
-        slices_left = kSubQueues;
-        stealing = false;
-        stolen = 0;
-        static_done = false;
+        spread = gridDim.x * (blockDim.x >> 5);     // ~2x the warps reading one side
+        const int block_log2 = kStrideLog2 ? kStrideLog2 + kGrabLog2 : 0;
+        main_pairs = kStrideLog2 ? (npairs >> block_log2) << block_log2 : 0;
+        tail_stride = kStrideLog2 ? (npairs - main_pairs) >> kGrabLog2 : 0;
         p = p1 = nstart = 0;
         nsize = 0;
         pending = false;
     }
-    // Queued pairs, and the [first, first + size) positions of a slice.
-    QRC_MEMBER qrc_u64 queued() const { return npairs - nstatic; }
-    QRC_MEMBER qrc_u64 slice_first(int k) const { return queued() * (qrc_u64)k / kSubQueues; }
-    QRC_MEMBER qrc_u64 slice_size(int k) const { return slice_first(k + 1) - slice_first(k); }
-    QRC_MEMBER qrc_u32* counter(int s, int k) const { return map + O_QUEUES + 32 * (s * kSubQueues + k); }
-    // Grab size when `seen` positions of the current slice are taken.
+    // Grab size when `seen` pairs of this side are already taken.
     QRC_MEMBER qrc_u32 grab_size(qrc_u64 seen) const {
         if (stealing) return 1u;                 // the other side is in its tail
-        const qrc_u64 size = slice_size(slice);
-        const qrc_u64 left = size > seen ? size - seen : 0;
-        const qrc_u64 s = left * kSubQueues / spread;
+        const qrc_u64 left = npairs > seen ? npairs - seen : 0;
+        const qrc_u64 s = left / spread;
         return s >= kMaxGrab ? kMaxGrab : (s < 1 ? 1u : (qrc_u32)s);
     }
-    // Lane 0 requests the grab that follows [start, start + size) in the
-    // current slice; the reply is read by the next call that runs out of pairs.
+    // Lane 0 requests the grab that follows [start, start + size); the reply
+    // is read by the next call that runs out of pairs.
     QRC_MEMBER void request(int lane, qrc_u64 start, qrc_u32 size) {
         if (lane == 0) {
             nsize = grab_size(start + size);
-            nstart = atomicAdd(counter(qside, slice), nsize);
+            nstart = atomicAdd(queue, nsize);
         }
         pending = true;
     }
-    // Makes positions [st, st + sz) of the current slice current; false when
-    // the slice is exhausted.
+    // Makes [st, st + sz) current; returns false when the queue is exhausted.
     QRC_MEMBER bool adopt(int lane, qrc_u64 st, qrc_u32 sz) {
-        const qrc_u64 size = slice_size(slice);
-        if (st >= size) { p = p1 = 0; pending = false; return false; }
+        if (st >= npairs) { p = p1 = 0; pending = false; return false; }
         p = st;
-        p1 = st + sz < size ? st + sz : size;
+        p1 = st + sz < npairs ? st + sz : npairs;
         request(lane, st, sz);
         return true;
     }
-    // First request on the current slice (all lanes).
-    QRC_MEMBER bool start_slice(int lane) {
+    QRC_MEMBER void begin(int lane) {
         const qrc_u32 sz = grab_size(0);
         qrc_u64 st = 0;
-        if (lane == 0) st = atomicAdd(counter(qside, slice), sz);
+        if (lane == 0) st = atomicAdd(queue, sz);
         st = __shfl_sync(0xFFFFFFFFu, st, 0);
-        return adopt(lane, st, sz);
+        adopt(lane, st, sz);
     }
-    // Moves to the next slice with work, then to the other side's slices;
-    // false when nothing is left for this warp.
-    QRC_MEMBER bool advance(int lane) {
-        if (queued() == 0) return false;
-        while (true) {
-            if (--slices_left > 0) {
-                slice = (slice + 1) % kSubQueues;
-            } else {
-#if QRC_STEAL
-                if (stealing) return false;
-                stealing = true;          // help the other side finish its slices
-                qside ^= 1;
-                side ^= 1;
-                slices_left = kSubQueues;
-                slice = (int)(warp_id % kSubQueues);
-#else
-                return false;
-#endif
-            }
-            if (start_slice(lane)) return true;
-        }
-    }
-    // Issues the first queue request without waiting for it: its reply is
-    // read after the warp's static-round chunk.
-    QRC_MEMBER void begin(int lane) {
-        if (queued() == 0) return;
-        if (lane == 0) {
-            nsize = grab_size(0);
-            nstart = atomicAdd(counter(qside, slice), nsize);
-        }
-        pending = true;
-    }
-    // Pair index of queue position c of a slice with `size` positions: a
-    // bijection of [0, size).  Inside a block of 2^(stride+grab) positions,
-    // position r goes to (r mod grab) * 2^stride + r / grab; the last, partial
-    // block uses the stride that fits it; positions past that map to themselves.
-    QRC_MEMBER static qrc_u64 pair_of(qrc_u64 c, qrc_u64 size) {
+    // Pair index of queue position c: a bijection of [0, npairs).  Inside a
+    // block of 2^(stride+grab) positions, position r goes to pair
+    // (r mod grab) * 2^stride + r / grab; the last, partial block uses the
+    // stride that fits it; positions past that map to themselves.
+    QRC_MEMBER qrc_u64 pair_of(qrc_u64 c) const {
         if (kStrideLog2 == 0) return c;
         const qrc_u64 G1 = (1ull << kGrabLog2) - 1;
-        const int block_log2 = kStrideLog2 + kGrabLog2;
-        const qrc_u64 main_pairs = (size >> block_log2) << block_log2;
         if (c < main_pairs) {
+            const int block_log2 = kStrideLog2 + kGrabLog2;
             const qrc_u64 r = c & ((1ull << block_log2) - 1);
             return (c - r) + ((r & G1) << kStrideLog2) + (r >> kGrabLog2);
         }
-        const qrc_u64 tail_stride = (size - main_pairs) >> kGrabLog2;
         const qrc_u64 r = c - main_pairs;
         if (r < (tail_stride << kGrabLog2)) return main_pairs + (r & G1) * tail_stride + (r >> kGrabLog2);
         return c;
     }
     QRC_MEMBER qrc_u64 next(int lane) {
-        if (!static_done) {
-            static_done = true;
-            if ((qrc_u64)warp_id < 2 * nstatic)      // one chunk of the static round
-                return lo + (qrc_u64)(warp_id >> 1) * (2 * C) + ((warp_id & 1) ? C : 0ull);
-        }
         if (p >= p1) {
-            if (!pending) {
-                if (!advance(lane)) return 0;
-            } else {
-                const qrc_u64 st = __shfl_sync(0xFFFFFFFFu, nstart, 0);
-                const qrc_u32 sz = __shfl_sync(0xFFFFFFFFu, nsize, 0);
-                if (!adopt(lane, st, sz) && !advance(lane)) return 0;
+            if (!pending) return 0;
+            const qrc_u64 st = __shfl_sync(0xFFFFFFFFu, nstart, 0);
+            const qrc_u32 sz = __shfl_sync(0xFFFFFFFFu, nsize, 0);
+            if (!adopt(lane, st, sz)) {
+#if QRC_STEAL
+                if (stealing) return 0;
+                // Own side done: help the other side finish (its halves are
+                // homed on the other die, so these reads cross it).
+                stealing = true;
+                side ^= 1;
+                queue = other;
+                begin(lane);
+                if (p >= p1) return 0;
+#else
+                return 0;
+#endif
             }
         }
-        const qrc_u64 pair = nstatic + slice_first(slice) + pair_of(p, slice_size(slice));
-        const qrc_u64 pa = lo + pair * (2 * C);
+        const qrc_u64 pa = lo + pair_of(p) * (2 * C);
         p++;
         stolen += stealing ? 1u : 0u;
         int pbit = 0;

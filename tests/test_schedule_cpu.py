@@ -44,49 +44,26 @@ def test_aligned_grab_spreads_and_neighbours_are_adjacent():
     assert np.all(np.diff(firsts) == 1)
 
 
-SUBQUEUES = 4
-
-
-def schedule_chunks(npairs, warps, rng):
-    """Chunk indices (2*pair + half) read by the walk, as SideWalk does it:
-    the static round hands chunk h to global warp h for the first
-    min(npairs, warps/2) pairs; the rest is split into SUBQUEUES slices per
-    side, each taken in random grab sizes and mapped through pair_of().
-    Returns (side, chunk) for every chunk read; `half` for queued pairs is
-    the oracle's choice for that side."""
-    nstatic = min(npairs, warps // 2)
-    out = [(None, h) for h in range(2 * nstatic)]
-    queued = npairs - nstatic
-    for side in (0, 1):
-        for k in range(SUBQUEUES):
-            first = queued * k // SUBQUEUES
-            size = queued * (k + 1) // SUBQUEUES - first
-            c = 0
-            while c < size:
-                g = int(rng.integers(1, 9))
-                for q in range(c, min(c + g, size)):
-                    out.append((side, nstatic + first + pair_of(q, size)))
-                c += g
-    return out, nstatic
-
-
-@pytest.mark.parametrize("npairs", [1, 5, 100, 2368, 2369, 5000, 40000])
-def test_static_round_and_slices_cover_every_byte_once(oracle, npairs):
-    """Any mask / page bits and any grab split: every chunk exactly once."""
-    rng = np.random.default_rng(npairs)
+def test_two_sides_cover_every_byte_once(oracle):
+    """Side 0 reads, for each pair, the half homed on side 0 and side 1 the
+    other half, for any mask / page bits and any grab split."""
+    rng = np.random.default_rng(0)
     C = 4096
-    warps = 4736
-    base = int(rng.integers(0, 1 << 30)) & ~(2 * C - 1)
-    mask = (int(rng.integers(0, 1 << 21)) & ~0xFFF) | 0x1000
-    page_bits = rng.integers(0, 2, size=(npairs * 2 * C >> 21) + 2)
-    covered = np.zeros(2 * npairs, dtype=np.int32)
-    reads, nstatic = schedule_chunks(npairs, warps, rng)
-    for side, x in reads:
-        if side is None:                      # static round: chunk index given directly
-            covered[x] += 1
-            continue
-        p = x
-        addr = base + p * 2 * C
-        pb = int(page_bits[(addr - (base & ~((1 << 21) - 1))) >> 21])
-        covered[2 * p + oracle.pair_half(addr, mask, pb, side)] += 1
-    assert np.all(covered == 1)
+    for trial in range(20):
+        npairs = int(rng.integers(1, 3000))
+        base = int(rng.integers(0, 1 << 30)) & ~(2 * C - 1)
+        mask = (int(rng.integers(0, 1 << 21)) & ~0xFFF) | 0x1000
+        page_bits = rng.integers(0, 2, size=(npairs * 2 * C >> 21) + 2)
+        covered = np.zeros(2 * npairs, dtype=np.int8)          # chunk granularity
+        for side in (0, 1):
+            c = 0
+            while c < npairs:                                    # random grab sizes
+                size = int(rng.integers(1, 9))
+                for q in range(c, min(c + size, npairs)):
+                    p = pair_of(q, npairs)
+                    addr = base + p * 2 * C
+                    pb = int(page_bits[(addr - (base & ~((1 << 21) - 1))) >> 21])
+                    half = oracle.pair_half(addr, mask, pb, side)
+                    covered[2 * p + half] += 1
+                c += size
+        assert np.all(covered == 1), trial
