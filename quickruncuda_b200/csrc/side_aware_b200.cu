@@ -115,6 +115,11 @@ constexpr int kMaxSm = 256;
 #ifndef QRC_FINISH
 #define QRC_FINISH 1
 #endif
+//   QRC_SHARES     1: static per-SM shares for 7/8 of the pairs (see
+//                  reduce_run); 0: every pair through the side queues
+#ifndef QRC_SHARES
+#define QRC_SHARES 1
+#endif
 //   QRC_TIMELINE   1: each CTA of a reduction records its start and end
 //                  %globaltimer, side, SM and the chunks it read from the other
 //                  side's queue in the map (words O_TIMELINE + 4*CTA, up to
@@ -126,7 +131,7 @@ constexpr int kGrabLog2 = QRC_MAX_GRAB >= 16 ? 4 : QRC_MAX_GRAB >= 8 ? 3 : QRC_M
 constexpr int kVerifyRandom = 64;
 constexpr int kVerifyCal = 8;                    // anchor + partner re-probes in verification
 constexpr int kCalProbes = 16;                   // per side, calibration wave
-constexpr int kDiagPages = 2048;                 // raw page latencies kept for diagnostics
+constexpr int kDiagPages = 1024;                 // raw page latencies kept for diagnostics
 constexpr qrc_u32 kDefaultPageWords = 1024;      // page-bit capacity (32768 pages = 64 GiB)
 
 // Side map layout (32-bit words).  The buffer must start zeroed.
@@ -140,9 +145,10 @@ enum : qrc_u32 {
     H_ERR = 96, H_ERR_ADDR_LO = 97, H_ERR_ADDR_HI = 98, H_WAIT_ERR = 99,
     H_COV_BYTES_LO = 100, H_COV_BYTES_HI = 101, H_COV_XOR_LO = 102, H_COV_XOR_HI = 103,
     O_BITLAT = 128,                                // 21 raw latencies of the mask probes
-    O_SM_SIDE = 256,                               // per SM: 0 unknown, 1 side 0, 2 side 1
+    O_SM_SIDE = 256,                               // per SM: 0 unknown, else 1 + side + 2 * index within side
     O_SM_LAT = 512,                                // per SM raw anchor latency (cycles)
     O_PAGE_LAT = 1024,                             // first kDiagPages raw page latencies
+    O_CLAIMS = 2048,                               // share marks: side * 128 + index within side
     O_TIMELINE = 3072,                             // QRC_TIMELINE: 4 words per CTA, 256 CTAs
     O_PAGE_BITS = 4096,                            // one bit per 2 MiB page
 };
@@ -298,7 +304,7 @@ QRC_DEV void discover(const void* A, qrc_u64 bytes, qrc_u32* map) {
             if (l == 0) { map[O_SM_SIDE + i] = 0; continue; }
             nsm++;
             const qrc_u32 side = (st == ST_OK && (float)l >= thr) ? 1u : 0u;
-            map[O_SM_SIDE + i] = 1u + side;
+            map[O_SM_SIDE + i] = 1u + side + 2u * (side ? n1 : n0);   // side and dense index within it
             if (side) n1++; else n0++;
         }
         map[H_NSM] = nsm; map[H_NSIDE0] = n0; map[H_NSIDE1] = n1;
@@ -594,75 +600,33 @@ QRC_DEV float e4m3_scale_from_amax(float amax) {
     return __fdiv_rn(448.0f, amax);
 }
 
-// Block-wide finish: warp redux, smem, one atomicMax, fenced ticket; the last
-// CTA publishes the result and resets the per-launch scratch.  With `scale_out`
-// it also publishes the e4m3 scale derived from the maximum.
-QRC_DEV void finish_block(qrc_u32 bits, qrc_u32* map, float* out, float* scale_out) {
-    __shared__ qrc_u32 s_w[32];
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, W = blockDim.x >> 5;
-    bits = __reduce_max_sync(0xFFFFFFFFu, bits);
-    if (lane == 0) s_w[warp] = bits;
-    __syncthreads();
-    if (warp == 0) {
-        qrc_u32 v = lane < W ? s_w[lane] : 0u;
-        v = __reduce_max_sync(0xFFFFFFFFu, v);
-        if (lane == 0) {
-#if QRC_FINISH == 1
-            // The block's maximum goes out as a fire-and-forget reduction;
-            // the ticket increment has release semantics (it is ordered after
-            // that reduction) and acquire semantics (the last CTA then sees
-            // every other CTA's reduction).
-            qrc_u32 t;
-            asm volatile("red.relaxed.gpu.global.max.u32 [%0], %1;" :: "l"(&map[H_ACC]), "r"(v) : "memory");
-            asm volatile("atom.acq_rel.gpu.global.inc.u32 %0, [%1], %2;"
-                         : "=r"(t) : "l"(&map[H_RUN_TICKET]), "r"(gridDim.x - 1) : "memory");
-            if (t == gridDim.x - 1) {
-#else
-            atomicMax(&map[H_ACC], v);
-            __threadfence();
-            const qrc_u32 t = atomicInc(&map[H_RUN_TICKET], gridDim.x - 1);
-            if (t == gridDim.x - 1) {
-                __threadfence();
-#endif
-                qrc_u32 r = atomicExch(&map[H_ACC], 0u);
-                map[H_QUEUE0] = 0u;
-                map[H_QUEUE1] = 0u;
-                if (map[H_WAIT_ERR]) r = 0x7FFFFFFFu;   // a bounded wait gave up: no valid maximum
-                out[0] = __uint_as_float(r);
-#if QRC_TIMELINE
-                qrc_u64 t_fin;
-                asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_fin));
-                map[O_TIMELINE + 1023] = (qrc_u32)t_fin;      // end of the launch's last CTA
-#endif
-                if (scale_out) scale_out[0] = e4m3_scale_from_amax(__uint_as_float(r));
-            }
-        }
-    }
-}
-
-// Per-warp walk over the pairs of one side.  Built from the side map (or
-// without one: mask 0, page bits 0), it hands each call the address of the
-// next C-byte chunk this warp must read.  Work comes from the side's queue, a
-// counter of pairs: a warp adds its grab size and owns the pairs between the
-// old and new value.  Grabs are guided: QRC_MAX_GRAB pairs while plenty are
-// left, shrinking to one pair as the queue empties, so all warps of a side
-// finish within about one chunk of each other.  The next grab is requested
-// while the current one is read.  All lanes call next() together (it
-// broadcasts lane 0's atomics).
+// Per-warp walk over the pairs of one side, for the pairs the static shares
+// leave to the queues ([qbase, npairs)).  Built from the side map (or without
+// one: mask 0, page bits 0), it hands each call the address of the next
+// C-byte chunk this warp must read.  Work comes from the side's queue, a
+// counter of positions: a warp adds its grab size and owns the positions
+// between the old and new value; positions map to pairs through the
+// interleave of pair_of().  For every pair the warp reads the half homed on
+// its own side, so the two sides' queues together read every queued byte
+// once whatever the map says.  Grabs are guided: QRC_MAX_GRAB pairs while
+// plenty are left, shrinking to one pair as the queue empties.  The first
+// request is issued by begin() without waiting (its reply is read on the
+// first next()), and each later request while the current grab is read.
+// All lanes call begin()/next() together (they broadcast lane 0's atomics).
 struct SideWalk {
-    qrc_u64 lo, hi, C, mask, page_base, npairs, p, p1, nstart;
-    qrc_u64 main_pairs, tail_stride;   // interleave: full blocks, stride of the last block
+    qrc_u64 lo, hi, C, mask, page_base, npairs, qbase, nq, p, p1, nstart;
+    qrc_u64 main_pairs, tail_stride;   // interleave over the nq queued pairs
     const qrc_u32* page_bits;
     qrc_u32* queue;
     qrc_u32* other;
     qrc_u32 nsize, spread;
-    int side, use_page_bits, flip;
-    bool pending, stealing;
+    int side, sm_index, use_page_bits, flip;
+    bool aware, pending, stealing;
     qrc_u32 stolen;                    // chunks read through the other side's queue
 
     QRC_MEMBER void setup(qrc_u64 a, qrc_u64 end, qrc_u32* map, qrc_u32 mode) {
         const qrc_u64 mb = map_base(map), mbytes = map_bytes(map);
-        const bool aware = map[H_MAGIC] == kMagic && map[H_STATUS] == ST_OK && a >= mb && end <= mb + mbytes;
+        aware = map[H_MAGIC] == kMagic && map[H_STATUS] == ST_OK && a >= mb && end <= mb + mbytes;
         mask = aware ? map[H_MASK] : 0u;
         C = 1ull << (aware ? (int)map[H_CHUNK_LOG2] : 12);
         page_base = mb & ~(kPage - 1);
@@ -671,7 +635,8 @@ struct SideWalk {
         flip = mode == MODE_WRONG_SIDE;
         const qrc_u32 sm = smid();
         const qrc_u32 lab = (aware && sm < (qrc_u32)kMaxSm) ? map[O_SM_SIDE + sm] : 0u;
-        side = lab ? (int)(lab - 1) : (int)(blockIdx.x & 1);
+        side = lab ? (int)((lab - 1) & 1) : (int)(blockIdx.x & 1);
+        sm_index = lab ? (int)((lab - 1) >> 1) : -1;
         queue = &map[side ? H_QUEUE1 : H_QUEUE0];
         other = &map[side ? H_QUEUE0 : H_QUEUE1];
         stealing = false;
@@ -682,22 +647,38 @@ struct SideWalk {
         if (hi <= lo) { lo = end; hi = end; }
         npairs = (hi - lo) / PAIR;
         spread = gridDim.x * (blockDim.x >> 5);     // ~2x the warps reading one side
-        const int block_log2 = kStrideLog2 ? kStrideLog2 + kGrabLog2 : 0;
-        main_pairs = kStrideLog2 ? (npairs >> block_log2) << block_log2 : 0;
-        tail_stride = kStrideLog2 ? (npairs - main_pairs) >> kGrabLog2 : 0;
+        set_queued(0);
         p = p1 = nstart = 0;
         nsize = 0;
         pending = false;
     }
-    // Grab size when `seen` pairs of this side are already taken.
+    // The queues cover pairs [first, npairs).
+    QRC_MEMBER void set_queued(qrc_u64 first) {
+        qbase = first;
+        nq = npairs - first;
+        const int block_log2 = kStrideLog2 ? kStrideLog2 + kGrabLog2 : 0;
+        main_pairs = kStrideLog2 ? (nq >> block_log2) << block_log2 : 0;
+        tail_stride = kStrideLog2 ? (nq - main_pairs) >> kGrabLog2 : 0;
+    }
+    // Address of the chunk of `pair` homed on side `s`.
+    QRC_MEMBER qrc_u64 chunk_of(qrc_u64 pair, int s) const {
+        const qrc_u64 pa = lo + pair * (2 * C);
+        int pbit = 0;
+        if (use_page_bits) {
+            const qrc_u64 pg = (pa - page_base) >> 21;
+            pbit = (page_bits[pg >> 5] >> (pg & 31)) & 1;
+        }
+        const int first_side = parity64(pa & mask) ^ pbit ^ flip;
+        return pa + ((first_side != s) ? C : 0ull);
+    }
+    // Grab size when `seen` queued positions of this side are taken.
     QRC_MEMBER qrc_u32 grab_size(qrc_u64 seen) const {
         if (stealing) return 1u;                 // the other side is in its tail
-        const qrc_u64 left = npairs > seen ? npairs - seen : 0;
+        const qrc_u64 left = nq > seen ? nq - seen : 0;
         const qrc_u64 s = left / spread;
         return s >= kMaxGrab ? kMaxGrab : (s < 1 ? 1u : (qrc_u32)s);
     }
-    // Lane 0 requests the grab that follows [start, start + size); the reply
-    // is read by the next call that runs out of pairs.
+    // Lane 0 requests the grab that follows [start, start + size).
     QRC_MEMBER void request(int lane, qrc_u64 start, qrc_u32 size) {
         if (lane == 0) {
             nsize = grab_size(start + size);
@@ -705,25 +686,29 @@ struct SideWalk {
         }
         pending = true;
     }
-    // Makes [st, st + sz) current; returns false when the queue is exhausted.
-    QRC_MEMBER bool adopt(int lane, qrc_u64 st, qrc_u32 sz) {
-        if (st >= npairs) { p = p1 = 0; pending = false; return false; }
+    // Makes positions [st, st + sz) current (and requests the next grab);
+    // an exhausted queue leaves nothing pending.
+    QRC_MEMBER void adopt(int lane, qrc_u64 st, qrc_u32 sz) {
+        if (st >= nq) { p = p1 = 0; pending = false; return; }
         p = st;
-        p1 = st + sz < npairs ? st + sz : npairs;
+        p1 = st + sz < nq ? st + sz : nq;
         request(lane, st, sz);
-        return true;
     }
+    // First request; does not wait for the reply.
     QRC_MEMBER void begin(int lane) {
-        const qrc_u32 sz = grab_size(0);
-        qrc_u64 st = 0;
-        if (lane == 0) st = atomicAdd(queue, sz);
-        st = __shfl_sync(0xFFFFFFFFu, st, 0);
-        adopt(lane, st, sz);
+        p = p1 = 0;
+        pending = false;
+        if (nq == 0) return;
+        if (lane == 0) {
+            nsize = grab_size(0);
+            nstart = atomicAdd(queue, nsize);
+        }
+        pending = true;
     }
-    // Pair index of queue position c: a bijection of [0, npairs).  Inside a
-    // block of 2^(stride+grab) positions, position r goes to pair
-    // (r mod grab) * 2^stride + r / grab; the last, partial block uses the
-    // stride that fits it; positions past that map to themselves.
+    // Pair index (within the queued region) of queue position c: a bijection
+    // of [0, nq).  Inside a block of 2^(stride+grab) positions, position r
+    // goes to (r mod grab) * 2^stride + r / grab; the last, partial block uses
+    // the stride that fits it; positions past that map to themselves.
     QRC_MEMBER qrc_u64 pair_of(qrc_u64 c) const {
         if (kStrideLog2 == 0) return c;
         const qrc_u64 G1 = (1ull << kGrabLog2) - 1;
@@ -737,35 +722,29 @@ struct SideWalk {
         return c;
     }
     QRC_MEMBER qrc_u64 next(int lane) {
-        if (p >= p1) {
-            if (!pending) return 0;
-            const qrc_u64 st = __shfl_sync(0xFFFFFFFFu, nstart, 0);
-            const qrc_u32 sz = __shfl_sync(0xFFFFFFFFu, nsize, 0);
-            if (!adopt(lane, st, sz)) {
+        while (p >= p1) {
+            if (!pending) {
 #if QRC_STEAL
-                if (stealing) return 0;
+                if (stealing || nq == 0) return 0;
                 // Own side done: help the other side finish (its halves are
                 // homed on the other die, so these reads cross it).
                 stealing = true;
                 side ^= 1;
                 queue = other;
                 begin(lane);
-                if (p >= p1) return 0;
+                continue;
 #else
                 return 0;
 #endif
             }
+            const qrc_u64 st = __shfl_sync(0xFFFFFFFFu, nstart, 0);
+            const qrc_u32 sz = __shfl_sync(0xFFFFFFFFu, nsize, 0);
+            adopt(lane, st, sz);
         }
-        const qrc_u64 pa = lo + pair_of(p) * (2 * C);
+        const qrc_u64 pair = qbase + pair_of(p);
         p++;
         stolen += stealing ? 1u : 0u;
-        int pbit = 0;
-        if (use_page_bits) {
-            const qrc_u64 pg = (pa - page_base) >> 21;
-            pbit = (page_bits[pg >> 5] >> (pg & 31)) & 1;
-        }
-        const int first_side = parity64(pa & mask) ^ pbit ^ flip;
-        return pa + ((first_side != side) ? C : 0ull);
+        return chunk_of(pair, side);
     }
 };
 
@@ -889,9 +868,82 @@ QRC_DEV typename Op::Acc bulk_walk(typename Op::Acc acc, SideWalk& w, int S, qrc
     return acc;
 }
 
-// The reduction over n elements at A (element type given by Op).  Uses the
-// bulk staging when the launch provides dynamic shared memory for at least two
-// slots per warp, register loads otherwise.
+// Sum of the checked build's per-thread coverage counters into the map.
+#ifdef QRC_CHECKED
+QRC_DEV void cov_flush(CheckState& cs, int lane, qrc_u32* map) {
+    qrc_u64 b = cs.bytes, x = cs.xr;
+    for (int o = 16; o > 0; o >>= 1) {
+        b += __shfl_xor_sync(0xFFFFFFFFu, b, o);
+        x ^= __shfl_xor_sync(0xFFFFFFFFu, x, o);
+    }
+    if (lane == 0) {
+        atomicAdd((unsigned long long*)&map[H_COV_BYTES_LO], b);
+        atomicXor((unsigned long long*)&map[H_COV_XOR_LO], x);
+    }
+    cs.bytes = 0; cs.xr = 0;
+}
+#endif
+
+// Maximum of `bits` over the block, returned to every thread.
+QRC_DEV qrc_u32 block_max(qrc_u32 bits) {
+    __shared__ qrc_u32 s_w[32];
+    __shared__ qrc_u32 s_res;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, W = blockDim.x >> 5;
+    bits = __reduce_max_sync(0xFFFFFFFFu, bits);
+    if (lane == 0) s_w[warp] = bits;
+    __syncthreads();
+    if (warp == 0) {
+        qrc_u32 v = lane < W ? s_w[lane] : 0u;
+        v = __reduce_max_sync(0xFFFFFFFFu, v);
+        if (lane == 0) s_res = v;
+    }
+    __syncthreads();
+    return s_res;
+}
+
+// Static shares (see reduce_run).  Share (s, k) of the pairs [0, R) is the
+// chunk homed on side s of every pair j * K_s + k.
+struct Shares {
+    qrc_u32 K[2];
+    qrc_u64 R;
+    bool on;
+};
+
+// Reads share (s, k) with all warps of the block.
+template <class Op>
+QRC_DEV typename Op::Acc read_share(typename Op::Acc acc, const SideWalk& w, const Shares& sh, int s, int k,
+                                    int lane QRC_CS_PARAM) {
+    const int warp = threadIdx.x >> 5, W = blockDim.x >> 5;
+    const int n512 = (int)(w.C >> 9);
+    for (qrc_u64 j = warp;; j += W) {
+        const qrc_u64 pair = j * sh.K[s] + (qrc_u64)k;
+        if (pair >= sh.R) break;
+        acc = chunk_warp<Op>(acc, w.chunk_of(pair, s), n512, lane QRC_CS_ARG);
+    }
+    return acc;
+}
+
+// The reduction over n elements at A (element type given by Op).
+//
+// Side-aware path (modes 0-2), register loads:
+//   * Static shares: discovery gave every SM its side s and a dense index k
+//     among the K_s SMs of that side.  The first R = 7/8 of the pairs are
+//     split like the reference splits all of them (tests/side_aware.cu:280-326):
+//     the CTA on SM (s, k) reads the side-s chunk of pairs j*K_s + k, with
+//     consecutive j going to its consecutive warps.  No atomics; all SMs of a
+//     side sweep one compact window.  The CTA marks its share with a plain
+//     store.
+//   * The last 1/8 of the pairs go through the side queues (SideWalk), whose
+//     first request is issued before the share is read; a side that runs out
+//     helps the other (QRC_STEAL).  This absorbs uneven SM counts per side.
+//   * A maximum does not change when an element is read twice, so two CTAs on
+//     one SM only cost time.  A share nobody marked (an SM that got no CTA,
+//     e.g. a grid smaller than the GPU) is read by the last CTA after the
+//     ticket, before it publishes: every element is still read.
+//   * Shares are used when one CTA fills an SM (1024 threads, or a block with
+//     the bulk ring's shared memory) and there is a valid side map.
+// Bulk pipeline (dynamic shared memory for >= 2 slots per warp): queues only.
+// Mode 3: side-agnostic grid-stride stream.
 template <class Op>
 QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, float* out, float* scale_out, qrc_u32 mode) {
     const qrc_u64 a = (qrc_u64)A, bytes = n * (qrc_u64)Op::kElem, end = a + bytes;
@@ -901,6 +953,11 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, float* out, floa
     CheckState cs{a, end, 0ull, 0ull, map};
 #endif
     qrc_u64 lo, hi;   // body [lo, hi); edges [a, lo) and [hi, end)
+    SideWalk w;
+    Shares sh;
+    sh.on = false;
+    sh.R = 0;
+    sh.K[0] = sh.K[1] = 0;
 
     if (mode == MODE_STREAM) {
         // Side-agnostic grid-stride stream over the 16-byte aligned body.
@@ -923,15 +980,27 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, float* out, floa
         }
         griddep_launch_dependents();
     } else {
-        SideWalk w;
         w.setup(a, end, map, mode);       // reads only the map header, which reductions never write
         lo = w.lo; hi = w.hi;
+        const int S = bulk_slots_per_warp(dynamic_smem_size(), W);
+        sh.on = QRC_SHARES && w.aware && S < 2 &&
+                (blockDim.x == 1024 || dynamic_smem_size() > 116u * 1024u);
+        if (sh.on) {
+            sh.K[0] = map[H_NSIDE0];
+            sh.K[1] = map[H_NSIDE1];
+            sh.on = sh.K[0] > 0 && sh.K[1] > 0 && sh.K[0] <= 128 && sh.K[1] <= 128;
+        }
+        if (sh.on) {
+            sh.R = w.npairs - w.npairs / 8;
+            w.set_queued(sh.R);
+        }
         griddep_wait();                   // the queues and accumulator of the previous launch are reset
 #if QRC_TIMELINE
         qrc_u64 t_start;
         asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_start));
 #endif
-        const int S = bulk_slots_per_warp(dynamic_smem_size(), W);
+        const int own_side = w.side, own_k = w.sm_index;
+        const bool own = sh.on && own_k >= 0 && (qrc_u32)own_k < sh.K[own_side];
 #ifndef QRC_CHECKED
         if (S >= 2) {
             acc = bulk_walk<Op>(acc, w, S, map, lane, warp);
@@ -939,7 +1008,9 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, float* out, floa
 #endif
         {
             const int n512 = (int)(w.C >> 9);
-            w.begin(lane);
+            if (own && threadIdx.x == 0) *(volatile qrc_u32*)&map[O_CLAIMS + 128 * own_side + own_k] = 1u;
+            w.begin(lane);                // first queue request in flight during the share
+            if (own) acc = read_share<Op>(acc, w, sh, own_side, own_k, lane QRC_CS_ARG);
             for (qrc_u64 chunk = w.next(lane); chunk; chunk = w.next(lane))
                 acc = chunk_warp<Op>(acc, chunk, n512, lane QRC_CS_ARG);
         }
@@ -956,7 +1027,7 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, float* out, floa
             if (threadIdx.x == 0 && blockIdx.x < 256) {
                 qrc_u32* tl = map + O_TIMELINE + 4 * blockIdx.x;
                 tl[0] = (qrc_u32)t_start; tl[1] = (qrc_u32)t_end;
-                tl[2] = (qrc_u32)w.side | (s_stolen << 1); tl[3] = smid();
+                tl[2] = (qrc_u32)own_side | (s_stolen << 1); tl[3] = smid();
             }
         }
 #endif
@@ -965,21 +1036,78 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, float* out, floa
     // last CTA's last warp.
     if (blockIdx.x == 0 && warp == 0) acc = edge_warp<Op>(acc, a, lo, lane QRC_CS_ARG);
     if (blockIdx.x == gridDim.x - 1 && warp == W - 1) acc = edge_warp<Op>(acc, hi, end, lane QRC_CS_ARG);
-
 #ifdef QRC_CHECKED
-    {
-        qrc_u64 b = cs.bytes, x = cs.xr;
-        for (int o = 16; o > 0; o >>= 1) {
-            b += __shfl_xor_sync(0xFFFFFFFFu, b, o);
-            x ^= __shfl_xor_sync(0xFFFFFFFFu, x, o);
-        }
-        if (lane == 0) {
-            atomicAdd((unsigned long long*)&map[H_COV_BYTES_LO], b);
-            atomicXor((unsigned long long*)&map[H_COV_XOR_LO], x);
-        }
-    }
+    cov_flush(cs, lane, map);
 #endif
-    finish_block(Op::to_bits(acc), map, out, scale_out);
+
+    // ---- finish: block maximum, one reduction, ticket --------------------
+    const qrc_u32 v = block_max(Op::to_bits(acc));
+    __shared__ int s_last;
+    if (threadIdx.x == 0) {
+        qrc_u32 t;
+#if QRC_FINISH == 1
+        // The block's maximum goes out as a fire-and-forget reduction; the
+        // ticket increment has release semantics (ordered after it) and
+        // acquire semantics (the last CTA then sees every other CTA's
+        // reduction and share mark).
+        asm volatile("red.relaxed.gpu.global.max.u32 [%0], %1;" :: "l"(&map[H_ACC]), "r"(v) : "memory");
+        asm volatile("atom.acq_rel.gpu.global.inc.u32 %0, [%1], %2;"
+                     : "=r"(t) : "l"(&map[H_RUN_TICKET]), "r"(gridDim.x - 1) : "memory");
+#else
+        atomicMax(&map[H_ACC], v);
+        __threadfence();
+        t = atomicInc(&map[H_RUN_TICKET], gridDim.x - 1);
+#endif
+        __threadfence();
+        s_last = (t == gridDim.x - 1);
+    }
+    __syncthreads();
+    if (!s_last) return;
+
+    // ---- last CTA: unmarked shares, then publish ---------------------------
+    typename Op::Acc acc2 = Op::zero();
+    if (sh.on) {
+        __shared__ int s_share;
+        for (;;) {
+            if (warp == 0) {
+                int found = -1;
+                for (int base = 0; base < 256 && found < 0; base += 32) {
+                    const int id = base + lane, s = id >> 7, k = id & 127;
+                    const bool missing = (qrc_u32)k < sh.K[s] && __ldcg(&map[O_CLAIMS + id]) == 0u;
+                    const unsigned m = __ballot_sync(0xFFFFFFFFu, missing);
+                    if (m) found = base + __ffs(m) - 1;
+                }
+                if (lane == 0) {
+                    s_share = found;
+                    if (found >= 0) map[O_CLAIMS + found] = 1u;
+                }
+            }
+            __syncthreads();
+            const int pick = s_share;
+            __syncthreads();
+            if (pick < 0) break;
+            acc2 = read_share<Op>(acc2, w, sh, pick >> 7, pick & 127, lane QRC_CS_ARG);
+        }
+        for (int i = threadIdx.x; i < 256; i += blockDim.x) map[O_CLAIMS + i] = 0u;
+#ifdef QRC_CHECKED
+        cov_flush(cs, lane, map);
+#endif
+    }
+    const qrc_u32 v2 = block_max(Op::to_bits(acc2));
+    if (threadIdx.x == 0) {
+        qrc_u32 r = atomicExch(&map[H_ACC], 0u);
+        r = r > v2 ? r : v2;
+        map[H_QUEUE0] = 0u;
+        map[H_QUEUE1] = 0u;
+        if (map[H_WAIT_ERR]) r = 0x7FFFFFFFu;   // a bounded wait gave up: no valid maximum
+        out[0] = __uint_as_float(r);
+#if QRC_TIMELINE
+        qrc_u64 t_fin;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_fin));
+        map[O_TIMELINE + 1023] = (qrc_u32)t_fin;      // end of the launch's last CTA
+#endif
+        if (scale_out) scale_out[0] = e4m3_scale_from_amax(__uint_as_float(r));
+    }
 }
 
 }  // namespace qrc
