@@ -105,7 +105,7 @@ constexpr int kMaxSm = 256;
 //                  so all warps of a side work inside one compact window of
 //                  memory at a time; 0 maps positions to pairs in order
 #ifndef QRC_STRIDE_LOG2
-#define QRC_STRIDE_LOG2 11
+#define QRC_STRIDE_LOG2 0
 #endif
 #ifndef QRC_TIMELINE
 #define QRC_TIMELINE 0
@@ -901,8 +901,12 @@ QRC_DEV qrc_u32 block_max(qrc_u32 bits) {
     return s_res;
 }
 
-// Static shares (see reduce_run).  Share (s, k) of the pairs [0, R) is the
-// chunk homed on side s of every pair j * K_s + k.
+// Static shares (see reduce_run).  The pairs [0, R) are cut into blocks of
+// W consecutive pairs (W = warps per CTA); share (s, k) is the chunk homed on
+// side s of every pair in blocks k, k + K_s, k + 2 K_s, ..., warp w of the
+// CTA reading pair w of each block.  So an SM reads W adjacent pairs (one
+// 2 MiB page, mostly) per step while the K_s SMs of a side sweep one window of
+// K_s * W pairs together.
 struct Shares {
     qrc_u32 K[2];
     qrc_u64 R;
@@ -915,8 +919,8 @@ QRC_DEV typename Op::Acc read_share(typename Op::Acc acc, const SideWalk& w, con
                                     int lane QRC_CS_PARAM) {
     const int warp = threadIdx.x >> 5, W = blockDim.x >> 5;
     const int n512 = (int)(w.C >> 9);
-    for (qrc_u64 j = warp;; j += W) {
-        const qrc_u64 pair = j * sh.K[s] + (qrc_u64)k;
+    for (qrc_u64 b = (qrc_u64)k;; b += sh.K[s]) {
+        const qrc_u64 pair = b * W + warp;
         if (pair >= sh.R) break;
         acc = chunk_warp<Op>(acc, w.chunk_of(pair, s), n512, lane QRC_CS_ARG);
     }
@@ -1070,12 +1074,15 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, float* out, floa
         __shared__ int s_share;
         for (;;) {
             if (warp == 0) {
+                qrc_u32 mark[8];                  // all 256 marks in one round trip
+                #pragma unroll
+                for (int t = 0; t < 8; t++) mark[t] = __ldcg(&map[O_CLAIMS + 32 * t + lane]);
                 int found = -1;
-                for (int base = 0; base < 256 && found < 0; base += 32) {
-                    const int id = base + lane, s = id >> 7, k = id & 127;
-                    const bool missing = (qrc_u32)k < sh.K[s] && __ldcg(&map[O_CLAIMS + id]) == 0u;
-                    const unsigned m = __ballot_sync(0xFFFFFFFFu, missing);
-                    if (m) found = base + __ffs(m) - 1;
+                #pragma unroll
+                for (int t = 7; t >= 0; t--) {
+                    const int id = 32 * t + lane, s = id >> 7, k = id & 127;
+                    const unsigned m = __ballot_sync(0xFFFFFFFFu, (qrc_u32)k < sh.K[s] && mark[t] == 0u);
+                    if (m) found = 32 * t + __ffs(m) - 1;
                 }
                 if (lane == 0) {
                     s_share = found;
