@@ -120,6 +120,12 @@ constexpr int kMaxSm = 256;
 #ifndef QRC_SHARES
 #define QRC_SHARES 1
 #endif
+//   QRC_ACROSS     1: a warp takes its next 8 chunks together and loads slice k
+//                  of all 8 before slice k+1 (8 chunks in flight, one 512-byte
+//                  row of each); 0: one chunk at a time, all 8 rows
+#ifndef QRC_ACROSS
+#define QRC_ACROSS 0
+#endif
 //   QRC_TIMELINE   1: each CTA of a reduction records its start and end
 //                  %globaltimer, side, SM and the chunks it read from the other
 //                  side's queue in the map (words O_TIMELINE + 4*CTA, up to
@@ -593,6 +599,23 @@ QRC_DEV typename Op::Acc chunk_warp(typename Op::Acc acc, qrc_u64 chunk, int n51
     return acc;
 }
 
+// Reads up to 8 chunks with a warp, row k of every chunk before row k+1.
+template <class Op>
+QRC_DEV typename Op::Acc chunks_across(typename Op::Acc acc, const qrc_u64* ch, int m, int n512, int lane QRC_CS_PARAM) {
+    for (int k = 0; k < n512; k++) {
+        uint4 v[8];
+        #pragma unroll
+        for (int u = 0; u < 8; u++) {
+            v[u] = make_uint4(0u, 0u, 0u, 0u);
+            const qrc_u64 x = ch[u] + 16ull * lane + 512ull * k;
+            if (u < m) { QRC_CHECK(x, 16) v[u] = ld_stream16(x); }
+        }
+        #pragma unroll
+        for (int u = 0; u < 8; u++) acc = Op::step16(acc, v[u]);
+    }
+    return acc;
+}
+
 // scale for an e4m3 per-tensor quantize: 448 / amax with IEEE round-to-nearest
 // division; 1 when amax is 0 (empty / all-zero / all-NaN input) or infinite.
 QRC_DEV float e4m3_scale_from_amax(float amax) {
@@ -1015,8 +1038,23 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, float* out, floa
             if (own && threadIdx.x == 0) *(volatile qrc_u32*)&map[O_CLAIMS + 128 * own_side + own_k] = 1u;
             w.begin(lane);                // first queue request in flight during the share
             if (own) acc = read_share<Op>(acc, w, sh, own_side, own_k, lane QRC_CS_ARG);
+#if QRC_ACROSS
+            for (;;) {
+                qrc_u64 ch[8];
+                int m = 0;
+                #pragma unroll
+                for (int u = 0; u < 8; u++) {
+                    ch[u] = (m == u) ? w.next(lane) : 0ull;
+                    if (ch[u]) m++;
+                }
+                if (m == 0) break;
+                acc = chunks_across<Op>(acc, ch, m, n512, lane QRC_CS_ARG);
+                if (m < 8) break;
+            }
+#else
             for (qrc_u64 chunk = w.next(lane); chunk; chunk = w.next(lane))
                 acc = chunk_warp<Op>(acc, chunk, n512, lane QRC_CS_ARG);
+#endif
         }
         griddep_launch_dependents();
 #if QRC_TIMELINE
