@@ -924,28 +924,37 @@ QRC_DEV qrc_u32 block_max(qrc_u32 bits) {
     return s_res;
 }
 
-// Static shares (see reduce_run).  The pairs [0, R) are cut into blocks of
-// W consecutive pairs (W = warps per CTA); share (s, k) is the chunk homed on
-// side s of every pair in blocks k, k + K_s, k + 2 K_s, ..., warp w of the
-// CTA reading pair w of each block.  So an SM reads W adjacent pairs (one
-// 2 MiB page, mostly) per step while the K_s SMs of a side sweep one window of
-// K_s * W pairs together.
+// Static shares (see reduce_run).  M = min(K_0, K_1) SMs per side take part.
+// A 256-thread group reads the side-s chunks of 8 consecutive pairs at once:
+// thread t loads bytes 16t..16t+15 of each of the 8 chunks (eight 16-byte
+// loads in flight, all addresses computed on the spot).  Block b of 8 pairs
+// belongs to group b mod (M * G) of the side, G = groups per CTA, and group g
+// of the CTA on the SM with index k is group k * G + g, so each SM steps
+// through 8*G adjacent pairs while the M SMs of a side sweep one window.
+// Requires 4 KiB chunks (one 16-byte load per thread covers a chunk).
 struct Shares {
-    qrc_u32 K[2];
-    qrc_u64 R;
+    qrc_u32 M;
     bool on;
 };
 
-// Reads share (s, k) with all warps of the block.
 template <class Op>
-QRC_DEV typename Op::Acc read_share(typename Op::Acc acc, const SideWalk& w, const Shares& sh, int s, int k,
-                                    int lane QRC_CS_PARAM) {
-    const int warp = threadIdx.x >> 5, W = blockDim.x >> 5;
-    const int n512 = (int)(w.C >> 9);
-    for (qrc_u64 b = (qrc_u64)k;; b += sh.K[s]) {
-        const qrc_u64 pair = b * W + warp;
-        if (pair >= sh.R) break;
-        acc = chunk_warp<Op>(acc, w.chunk_of(pair, s), n512, lane QRC_CS_ARG);
+QRC_DEV typename Op::Acc read_share(typename Op::Acc acc, const SideWalk& w, const Shares& sh, int s, int k
+                                    QRC_CS_PARAM) {
+    const int G = blockDim.x >> 8, g = threadIdx.x >> 8, t = threadIdx.x & 255;
+    const qrc_u64 groups = (qrc_u64)sh.M * G, npairs = w.npairs;
+    for (qrc_u64 b = (qrc_u64)k * G + g; b * 8 < npairs; b += groups) {
+        uint4 v[8];
+        #pragma unroll
+        for (int j = 0; j < 8; j++) {
+            v[j] = make_uint4(0u, 0u, 0u, 0u);
+            const qrc_u64 pair = b * 8 + j;
+            if (pair < npairs) {
+                const qrc_u64 x = w.chunk_of(pair, s) + 16ull * t;
+                QRC_CHECK(x, 16) v[j] = ld_stream16(x);
+            }
+        }
+        #pragma unroll
+        for (int j = 0; j < 8; j++) acc = Op::step16(acc, v[j]);
     }
     return acc;
 }
@@ -954,21 +963,18 @@ QRC_DEV typename Op::Acc read_share(typename Op::Acc acc, const SideWalk& w, con
 //
 // Side-aware path (modes 0-2), register loads:
 //   * Static shares: discovery gave every SM its side s and a dense index k
-//     among the K_s SMs of that side.  The first R = 7/8 of the pairs are
-//     split like the reference splits all of them (tests/side_aware.cu:280-326):
-//     the CTA on SM (s, k) reads the side-s chunk of pairs j*K_s + k, with
-//     consecutive j going to its consecutive warps.  No atomics; all SMs of a
-//     side sweep one compact window.  The CTA marks its share with a plain
-//     store.
-//   * The last 1/8 of the pairs go through the side queues (SideWalk), whose
-//     first request is issued before the share is read; a side that runs out
-//     helps the other (QRC_STEAL).  This absorbs uneven SM counts per side.
+//     among the K_s SMs of that side.  With M = min(K_0, K_1), the CTA on SM
+//     (s, k < M) reads the side-s chunk of its share of every pair (see
+//     read_share); SMs with k >= M sit out, so both sides carry equal work per
+//     SM.  No atomics.  The CTA marks its share with a plain store.
 //   * A maximum does not change when an element is read twice, so two CTAs on
 //     one SM only cost time.  A share nobody marked (an SM that got no CTA,
 //     e.g. a grid smaller than the GPU) is read by the last CTA after the
 //     ticket, before it publishes: every element is still read.
 //   * Shares are used when one CTA fills an SM (1024 threads, or a block with
-//     the bulk ring's shared memory) and there is a valid side map.
+//     the bulk ring's shared memory), the block is a multiple of 256 threads,
+//     chunks are 4 KiB and there is a valid side map; otherwise every pair
+//     goes through the side queues (SideWalk).
 // Bulk pipeline (dynamic shared memory for >= 2 slots per warp): queues only.
 // Mode 3: side-agnostic grid-stride stream.
 template <class Op>
@@ -983,8 +989,7 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, float* out, floa
     SideWalk w;
     Shares sh;
     sh.on = false;
-    sh.R = 0;
-    sh.K[0] = sh.K[1] = 0;
+    sh.M = 0;
 
     if (mode == MODE_STREAM) {
         // Side-agnostic grid-stride stream over the 16-byte aligned body.
@@ -1010,24 +1015,21 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, float* out, floa
         w.setup(a, end, map, mode);       // reads only the map header, which reductions never write
         lo = w.lo; hi = w.hi;
         const int S = bulk_slots_per_warp(dynamic_smem_size(), W);
-        sh.on = QRC_SHARES && w.aware && S < 2 &&
+        sh.on = QRC_SHARES && w.aware && S < 2 && w.C == 4096 && (blockDim.x & 255) == 0 &&
                 (blockDim.x == 1024 || dynamic_smem_size() > 116u * 1024u);
         if (sh.on) {
-            sh.K[0] = map[H_NSIDE0];
-            sh.K[1] = map[H_NSIDE1];
-            sh.on = sh.K[0] > 0 && sh.K[1] > 0 && sh.K[0] <= 128 && sh.K[1] <= 128;
+            const qrc_u32 k0 = map[H_NSIDE0], k1 = map[H_NSIDE1];
+            sh.M = k0 < k1 ? k0 : k1;
+            sh.on = sh.M > 0 && sh.M <= 128;
         }
-        if (sh.on) {
-            sh.R = w.npairs - w.npairs / 8;
-            w.set_queued(sh.R);
-        }
+        if (sh.on) w.set_queued(w.npairs);    // the shares cover every pair
         griddep_wait();                   // the queues and accumulator of the previous launch are reset
 #if QRC_TIMELINE
         qrc_u64 t_start;
         asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_start));
 #endif
         const int own_side = w.side, own_k = w.sm_index;
-        const bool own = sh.on && own_k >= 0 && (qrc_u32)own_k < sh.K[own_side];
+        const bool own = sh.on && own_k >= 0 && (qrc_u32)own_k < sh.M;
 #ifndef QRC_CHECKED
         if (S >= 2) {
             acc = bulk_walk<Op>(acc, w, S, map, lane, warp);
@@ -1037,7 +1039,7 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, float* out, floa
             const int n512 = (int)(w.C >> 9);
             if (own && threadIdx.x == 0) *(volatile qrc_u32*)&map[O_CLAIMS + 128 * own_side + own_k] = 1u;
             w.begin(lane);                // first queue request in flight during the share
-            if (own) acc = read_share<Op>(acc, w, sh, own_side, own_k, lane QRC_CS_ARG);
+            if (own) acc = read_share<Op>(acc, w, sh, own_side, own_k QRC_CS_ARG);
 #if QRC_ACROSS
             for (;;) {
                 qrc_u64 ch[8];
@@ -1119,7 +1121,8 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, float* out, floa
                 #pragma unroll
                 for (int t = 7; t >= 0; t--) {
                     const int id = 32 * t + lane, s = id >> 7, k = id & 127;
-                    const unsigned m = __ballot_sync(0xFFFFFFFFu, (qrc_u32)k < sh.K[s] && mark[t] == 0u);
+                    const unsigned m = __ballot_sync(0xFFFFFFFFu, (qrc_u32)k < sh.M && mark[t] == 0u);
+                    (void)s;
                     if (m) found = 32 * t + __ffs(m) - 1;
                 }
                 if (lane == 0) {
@@ -1131,7 +1134,7 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, float* out, floa
             const int pick = s_share;
             __syncthreads();
             if (pick < 0) break;
-            acc2 = read_share<Op>(acc2, w, sh, pick >> 7, pick & 127, lane QRC_CS_ARG);
+            acc2 = read_share<Op>(acc2, w, sh, pick >> 7, pick & 127 QRC_CS_ARG);
         }
         for (int i = threadIdx.x; i < 256; i += blockDim.x) map[O_CLAIMS + i] = 0u;
 #ifdef QRC_CHECKED
