@@ -636,18 +636,16 @@ QRC_DEV float e4m3_scale_from_amax(float amax) {
 // request is issued by begin() without waiting (its reply is read on the
 // first next()), and each later request while the current grab is read.
 // All lanes call begin()/next() together (they broadcast lane 0's atomics).
-struct SideWalk {
-    qrc_u64 lo, hi, C, mask, page_base, npairs, qbase, nq, p, p1, nstart;
-    qrc_u64 main_pairs, tail_stride;   // interleave over the nq queued pairs
+// Geometry of one reduction: the pair range, the side map's mask and page
+// bits, and this SM's side and index within it.  chunk_of() turns a pair into
+// the address of its chunk homed on a given side.
+struct ChunkMap {
+    qrc_u64 lo, hi, C, mask, page_base, npairs;
     const qrc_u32* page_bits;
-    qrc_u32* queue;
-    qrc_u32* other;
-    qrc_u32 nsize, spread;
     int side, sm_index, use_page_bits, flip;
-    bool aware, pending, stealing;
-    qrc_u32 stolen;                    // chunks read through the other side's queue
+    bool aware;
 
-    QRC_MEMBER void setup(qrc_u64 a, qrc_u64 end, qrc_u32* map, qrc_u32 mode) {
+    QRC_MEMBER void setup(qrc_u64 a, qrc_u64 end, const qrc_u32* map, qrc_u32 mode) {
         const qrc_u64 mb = map_base(map), mbytes = map_bytes(map);
         aware = map[H_MAGIC] == kMagic && map[H_STATUS] == ST_OK && a >= mb && end <= mb + mbytes;
         mask = aware ? map[H_MASK] : 0u;
@@ -660,15 +658,40 @@ struct SideWalk {
         const qrc_u32 lab = (aware && sm < (qrc_u32)kMaxSm) ? map[O_SM_SIDE + sm] : 0u;
         side = lab ? (int)((lab - 1) & 1) : (int)(blockIdx.x & 1);
         sm_index = lab ? (int)((lab - 1) >> 1) : -1;
-        queue = &map[side ? H_QUEUE1 : H_QUEUE0];
-        other = &map[side ? H_QUEUE0 : H_QUEUE1];
-        stealing = false;
-        stolen = 0;
         const qrc_u64 PAIR = 2 * C;
         lo = (a + PAIR - 1) & ~(PAIR - 1);
         hi = end & ~(PAIR - 1);
         if (hi <= lo) { lo = end; hi = end; }
         npairs = (hi - lo) / PAIR;
+    }
+    // Address of the chunk of `pair` homed on side `s`.
+    QRC_MEMBER qrc_u64 chunk_of(qrc_u64 pair, int s) const {
+        const qrc_u64 pa = lo + pair * (2 * C);
+        int pbit = 0;
+        if (use_page_bits) {
+            const qrc_u64 pg = (pa - page_base) >> 21;
+            pbit = (page_bits[pg >> 5] >> (pg & 31)) & 1;
+        }
+        const int first_side = parity64(pa & mask) ^ pbit ^ flip;
+        return pa + ((first_side != s) ? C : 0ull);
+    }
+};
+
+struct SideWalk : ChunkMap {
+    qrc_u64 qbase, nq, p, p1, nstart;
+    qrc_u64 main_pairs, tail_stride;   // interleave over the nq queued pairs
+    qrc_u32* queue;
+    qrc_u32* other;
+    qrc_u32 nsize, spread;
+    bool pending, stealing;
+    qrc_u32 stolen;                    // chunks read through the other side's queue
+
+    QRC_MEMBER void setup(qrc_u64 a, qrc_u64 end, qrc_u32* map, qrc_u32 mode) {
+        ChunkMap::setup(a, end, map, mode);
+        queue = &map[side ? H_QUEUE1 : H_QUEUE0];
+        other = &map[side ? H_QUEUE0 : H_QUEUE1];
+        stealing = false;
+        stolen = 0;
         spread = gridDim.x * (blockDim.x >> 5);     // ~2x the warps reading one side
         set_queued(0);
         p = p1 = nstart = 0;
@@ -682,17 +705,6 @@ struct SideWalk {
         const int block_log2 = kStrideLog2 ? kStrideLog2 + kGrabLog2 : 0;
         main_pairs = kStrideLog2 ? (nq >> block_log2) << block_log2 : 0;
         tail_stride = kStrideLog2 ? (nq - main_pairs) >> kGrabLog2 : 0;
-    }
-    // Address of the chunk of `pair` homed on side `s`.
-    QRC_MEMBER qrc_u64 chunk_of(qrc_u64 pair, int s) const {
-        const qrc_u64 pa = lo + pair * (2 * C);
-        int pbit = 0;
-        if (use_page_bits) {
-            const qrc_u64 pg = (pa - page_base) >> 21;
-            pbit = (page_bits[pg >> 5] >> (pg & 31)) & 1;
-        }
-        const int first_side = parity64(pa & mask) ^ pbit ^ flip;
-        return pa + ((first_side != s) ? C : 0ull);
     }
     // Grab size when `seen` queued positions of this side are taken.
     QRC_MEMBER qrc_u32 grab_size(qrc_u64 seen) const {
@@ -938,7 +950,7 @@ struct Shares {
 };
 
 template <class Op>
-QRC_DEV typename Op::Acc read_share(typename Op::Acc acc, const SideWalk& w, const Shares& sh, int s, int k
+QRC_DEV typename Op::Acc read_share(typename Op::Acc acc, const ChunkMap& w, const Shares& sh, int s, int k
                                     QRC_CS_PARAM) {
     const int G = blockDim.x >> 8, g = threadIdx.x >> 8, t = threadIdx.x & 255;
     const qrc_u64 groups = (qrc_u64)sh.M * G, npairs = w.npairs;
@@ -986,7 +998,6 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, float* out, floa
     CheckState cs{a, end, 0ull, 0ull, map};
 #endif
     qrc_u64 lo, hi;   // body [lo, hi); edges [a, lo) and [hi, end)
-    SideWalk w;
     Shares sh;
     sh.on = false;
     sh.M = 0;
@@ -1012,50 +1023,60 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, float* out, floa
         }
         griddep_launch_dependents();
     } else {
-        w.setup(a, end, map, mode);       // reads only the map header, which reductions never write
-        lo = w.lo; hi = w.hi;
+        ChunkMap cm;
+        cm.setup(a, end, map, mode);      // reads only the map header, which reductions never write
+        lo = cm.lo; hi = cm.hi;
         const int S = bulk_slots_per_warp(dynamic_smem_size(), W);
-        sh.on = QRC_SHARES && w.aware && S < 2 && w.C == 4096 && (blockDim.x & 255) == 0 &&
+        sh.on = QRC_SHARES && cm.aware && S < 2 && cm.C == 4096 && (blockDim.x & 255) == 0 &&
                 (blockDim.x == 1024 || dynamic_smem_size() > 116u * 1024u);
         if (sh.on) {
             const qrc_u32 k0 = map[H_NSIDE0], k1 = map[H_NSIDE1];
             sh.M = k0 < k1 ? k0 : k1;
             sh.on = sh.M > 0 && sh.M <= 128;
         }
-        if (sh.on) w.set_queued(w.npairs);    // the shares cover every pair
-        griddep_wait();                   // the queues and accumulator of the previous launch are reset
+        griddep_wait();                   // the scratch of the previous launch is reset
 #if QRC_TIMELINE
         qrc_u64 t_start;
         asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_start));
+        qrc_u32 stolen = 0;
 #endif
-        const int own_side = w.side, own_k = w.sm_index;
-        const bool own = sh.on && own_k >= 0 && (qrc_u32)own_k < sh.M;
-#ifndef QRC_CHECKED
-        if (S >= 2) {
-            acc = bulk_walk<Op>(acc, w, S, map, lane, warp);
-        } else
-#endif
-        {
-            const int n512 = (int)(w.C >> 9);
-            if (own && threadIdx.x == 0) *(volatile qrc_u32*)&map[O_CLAIMS + 128 * own_side + own_k] = 1u;
-            w.begin(lane);                // first queue request in flight during the share
-            if (own) acc = read_share<Op>(acc, w, sh, own_side, own_k QRC_CS_ARG);
-#if QRC_ACROSS
-            for (;;) {
-                qrc_u64 ch[8];
-                int m = 0;
-                #pragma unroll
-                for (int u = 0; u < 8; u++) {
-                    ch[u] = (m == u) ? w.next(lane) : 0ull;
-                    if (ch[u]) m++;
-                }
-                if (m == 0) break;
-                acc = chunks_across<Op>(acc, ch, m, n512, lane QRC_CS_ARG);
-                if (m < 8) break;
+        if (sh.on) {
+            const int own_k = cm.sm_index;
+            if (own_k >= 0 && (qrc_u32)own_k < sh.M) {
+                if (threadIdx.x == 0) *(volatile qrc_u32*)&map[O_CLAIMS + 128 * cm.side + own_k] = 1u;
+                acc = read_share<Op>(acc, cm, sh, cm.side, own_k QRC_CS_ARG);
             }
+        } else {
+            SideWalk w;
+            w.setup(a, end, map, mode);
+#ifndef QRC_CHECKED
+            if (S >= 2) {
+                acc = bulk_walk<Op>(acc, w, S, map, lane, warp);
+            } else
+#endif
+            {
+                const int n512 = (int)(w.C >> 9);
+                w.begin(lane);
+#if QRC_ACROSS
+                for (;;) {
+                    qrc_u64 ch[8];
+                    int m = 0;
+                    #pragma unroll
+                    for (int u = 0; u < 8; u++) {
+                        ch[u] = (m == u) ? w.next(lane) : 0ull;
+                        if (ch[u]) m++;
+                    }
+                    if (m == 0) break;
+                    acc = chunks_across<Op>(acc, ch, m, n512, lane QRC_CS_ARG);
+                    if (m < 8) break;
+                }
 #else
-            for (qrc_u64 chunk = w.next(lane); chunk; chunk = w.next(lane))
-                acc = chunk_warp<Op>(acc, chunk, n512, lane QRC_CS_ARG);
+                for (qrc_u64 chunk = w.next(lane); chunk; chunk = w.next(lane))
+                    acc = chunk_warp<Op>(acc, chunk, n512, lane QRC_CS_ARG);
+#endif
+            }
+#if QRC_TIMELINE
+            stolen = w.stolen;
 #endif
         }
         griddep_launch_dependents();
@@ -1064,14 +1085,14 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, float* out, floa
             __shared__ qrc_u32 s_stolen;
             if (threadIdx.x == 0) s_stolen = 0;
             __syncthreads();
-            if (lane == 0 && w.stolen) atomicAdd(&s_stolen, w.stolen);
+            if (lane == 0 && stolen) atomicAdd(&s_stolen, stolen);
             __syncthreads();
             qrc_u64 t_end;
             asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_end));
             if (threadIdx.x == 0 && blockIdx.x < 256) {
                 qrc_u32* tl = map + O_TIMELINE + 4 * blockIdx.x;
                 tl[0] = (qrc_u32)t_start; tl[1] = (qrc_u32)t_end;
-                tl[2] = (qrc_u32)own_side | (s_stolen << 1); tl[3] = smid();
+                tl[2] = (qrc_u32)cm.side | (s_stolen << 1); tl[3] = smid();
             }
         }
 #endif
@@ -1111,6 +1132,8 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, float* out, floa
     // ---- last CTA: unmarked shares, then publish ---------------------------
     typename Op::Acc acc2 = Op::zero();
     if (sh.on) {
+        ChunkMap cm;
+        cm.setup(a, end, map, mode);
         __shared__ int s_share;
         for (;;) {
             if (warp == 0) {
@@ -1134,7 +1157,7 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, float* out, floa
             const int pick = s_share;
             __syncthreads();
             if (pick < 0) break;
-            acc2 = read_share<Op>(acc2, w, sh, pick >> 7, pick & 127 QRC_CS_ARG);
+            acc2 = read_share<Op>(acc2, cm, sh, pick >> 7, pick & 127 QRC_CS_ARG);
         }
         for (int i = threadIdx.x; i < 256; i += blockDim.x) map[O_CLAIMS + i] = 0u;
 #ifdef QRC_CHECKED
