@@ -646,16 +646,21 @@ struct ChunkMap {
     bool aware;
 
     QRC_MEMBER void setup(qrc_u64 a, qrc_u64 end, const qrc_u32* map, qrc_u32 mode) {
+        // Every header word is loaded unconditionally, so the loads go out
+        // together (one round trip) before anything depends on them.
+        const qrc_u32 sm = smid();
+        const qrc_u32 h_magic = map[H_MAGIC], h_status = map[H_STATUS], h_mask = map[H_MASK];
+        const qrc_u32 h_clog2 = map[H_CHUNK_LOG2];
         const qrc_u64 mb = map_base(map), mbytes = map_bytes(map);
-        aware = map[H_MAGIC] == kMagic && map[H_STATUS] == ST_OK && a >= mb && end <= mb + mbytes;
-        mask = aware ? map[H_MASK] : 0u;
-        C = 1ull << (aware ? (int)map[H_CHUNK_LOG2] : 12);
+        const qrc_u32 lab_raw = map[O_SM_SIDE + (sm & (qrc_u32)(kMaxSm - 1))];
+        aware = h_magic == kMagic && h_status == ST_OK && a >= mb && end <= mb + mbytes;
+        mask = aware ? h_mask : 0u;
+        C = 1ull << (aware ? (int)h_clog2 : 12);
         page_base = mb & ~(kPage - 1);
         page_bits = map + O_PAGE_BITS;
         use_page_bits = aware && mode != MODE_IGNORE_PAGE_BITS;
         flip = mode == MODE_WRONG_SIDE;
-        const qrc_u32 sm = smid();
-        const qrc_u32 lab = (aware && sm < (qrc_u32)kMaxSm) ? map[O_SM_SIDE + sm] : 0u;
+        const qrc_u32 lab = (aware && sm < (qrc_u32)kMaxSm) ? lab_raw : 0u;
         side = lab ? (int)((lab - 1) & 1) : (int)(blockIdx.x & 1);
         sm_index = lab ? (int)((lab - 1) >> 1) : -1;
         const qrc_u64 PAIR = 2 * C;
@@ -1159,11 +1164,16 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, float* out, floa
     if (!s_last) return;
 
     // ---- last CTA: unmarked shares, then publish ---------------------------
+    // Thread 0 takes the accumulator while warp 0 checks the share marks, in
+    // the same round trip; only a missing share costs more.
+    __shared__ qrc_u32 s_acc;
+    __shared__ int s_share;
+    if (threadIdx.x == 0) s_acc = atomicExch(&map[H_ACC], 0u);
     typename Op::Acc acc2 = Op::zero();
+    bool extra = false;
     if (sh.on) {
         ChunkMap cm;
         cm.setup(a, end, map, mode);
-        __shared__ int s_share;
         for (;;) {
             if (warp == 0) {
                 qrc_u32 mark[8];                  // all 256 marks in one round trip
@@ -1172,9 +1182,8 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, float* out, floa
                 int found = -1;
                 #pragma unroll
                 for (int t = 7; t >= 0; t--) {
-                    const int id = 32 * t + lane, s = id >> 7, k = id & 127;
+                    const int k = (32 * t + lane) & 127;
                     const unsigned m = __ballot_sync(0xFFFFFFFFu, (qrc_u32)k < sh.M && mark[t] == 0u);
-                    (void)s;
                     if (m) found = 32 * t + __ffs(m) - 1;
                 }
                 if (lane == 0) {
@@ -1186,16 +1195,19 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, float* out, floa
             const int pick = s_share;
             __syncthreads();
             if (pick < 0) break;
+            extra = true;
             acc2 = read_share<Op>(acc2, cm, sh, pick >> 7, pick & 127 QRC_CS_ARG);
         }
         for (int i = threadIdx.x; i < 256; i += blockDim.x) map[O_CLAIMS + i] = 0u;
 #ifdef QRC_CHECKED
         cov_flush(cs, lane, map);
 #endif
+    } else {
+        __syncthreads();
     }
-    const qrc_u32 v2 = block_max(Op::to_bits(acc2));
+    const qrc_u32 v2 = extra ? block_max(Op::to_bits(acc2)) : 0u;
     if (threadIdx.x == 0) {
-        qrc_u32 r = atomicExch(&map[H_ACC], 0u);
+        qrc_u32 r = s_acc;
         r = r > v2 ? r : v2;
         map[H_QUEUE0] = 0u;
         map[H_QUEUE1] = 0u;
