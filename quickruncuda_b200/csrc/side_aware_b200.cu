@@ -129,7 +129,9 @@ constexpr int kMaxSm = 256;
 //   QRC_TIMELINE   1: each CTA of a reduction records its start and end
 //                  %globaltimer, side, SM and the chunks it read from the other
 //                  side's queue in the map (words O_TIMELINE + 4*CTA, up to
-//                  256 CTAs), for diagnostics; off by default
+//                  256 CTAs); word O_TIMELINE + 1023 gets the time the last CTA
+//                  published, + 1022 the previous launch's; diagnostics, off by
+//                  default
 constexpr qrc_u32 kMaxGrab = QRC_MAX_GRAB;
 constexpr int kStrideLog2 = QRC_STRIDE_LOG2;
 static_assert((QRC_MAX_GRAB & (QRC_MAX_GRAB - 1)) == 0, "QRC_MAX_GRAB must be a power of two");
@@ -1073,6 +1075,8 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, float* out, floa
         qrc_u64 t_start;
         asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_start));
         qrc_u32 stolen = 0;
+        if (blockIdx.x == 0 && threadIdx.x == 0)       // previous launch's finish, before this one overwrites it
+            map[O_TIMELINE + 1022] = __ldcg(&map[O_TIMELINE + 1023]);
 #endif
         if (sh.on) {
             const int own_k = cm.sm_index;
@@ -1156,8 +1160,8 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, float* out, floa
         atomicMax(&map[H_ACC], v);
         __threadfence();
         t = atomicInc(&map[H_RUN_TICKET], gridDim.x - 1);
-#endif
         __threadfence();
+#endif
         s_last = (t == gridDim.x - 1);
     }
     __syncthreads();
@@ -1172,8 +1176,6 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, float* out, floa
     typename Op::Acc acc2 = Op::zero();
     bool extra = false;
     if (sh.on) {
-        ChunkMap cm;
-        cm.setup(a, end, map, mode);
         for (;;) {
             if (warp == 0) {
                 qrc_u32 mark[8];                  // all 256 marks in one round trip
@@ -1196,6 +1198,8 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, float* out, floa
             __syncthreads();
             if (pick < 0) break;
             extra = true;
+            ChunkMap cm;                      // only when a share was missed
+            cm.setup(a, end, map, mode);
             acc2 = read_share<Op>(acc2, cm, sh, pick >> 7, pick & 127 QRC_CS_ARG);
         }
         for (int i = threadIdx.x; i < 256; i += blockDim.x) map[O_CLAIMS + i] = 0u;

@@ -18,6 +18,7 @@
 //     (the reference's NVML sampler exists but is never enabled,
 //     QuickRunCUDA.cpp:291, utils/nvmlClass.h:275-302);
 //   * --json prints one JSON object with the measurements;
+//   * --dump-b FILE writes buffer B raw after the runs (kernel-file state);
 //   * --clock-speed and --server are not provided: this harness changes no
 //     GPU setting and is a one-shot process.
 // Errors print a message and exit non-zero (the reference exits from
@@ -119,7 +120,7 @@ struct Args {
     std::string cubinFile = "";
     std::string arch = "sm_100a";
     bool reuseCubin = false, timesPerRun = false, compileOnly = false, json = false;
-    std::string dumpC, dumpCFormat = "raw", loadC, referenceC;
+    std::string dumpC, dumpCFormat = "raw", loadC, referenceC, dumpB;
     float compareTolerance = 0.f;
     std::string fillA;
     double powerSeconds = 0.0;
@@ -140,7 +141,7 @@ void usage() {
         "  -0/-1/-2,--kernel-int-arg{0,1,2} V\n"
         "  -f,--kernel-filename F   -H,--header S   --reuse-cubin   --cubin F\n"
         "  --arch sm_100a|sm_100   --compile-only\n"
-        "  --dump-c F   --dump-c-format raw|int_csv|float_csv   --load-c F\n"
+        "  --dump-c F   --dump-c-format raw|int_csv|float_csv   --load-c F   --dump-b F\n"
         "  --reference-c F   --compare-tolerance X\n"
         "  --fill-a uniform:SEED[:OUTLIER] | normal:SEED[:SIGMA]\n"
         "  --power-seconds S   --json   --device N\n");
@@ -195,6 +196,7 @@ Args parse(int argc, char** argv) {
         else if (f == "--compile-only") a.compileOnly = true;
         else if (f == "--dump-c") a.dumpC = need(i);
         else if (f == "--dump-c-format") a.dumpCFormat = need(i);
+        else if (f == "--dump-b") a.dumpB = need(i);
         else if (f == "--load-c") a.loadC = need(i);
         else if (f == "--reference-c") a.referenceC = need(i);
         else if (f == "--compare-tolerance") a.compareTolerance = std::stof(need(i));
@@ -555,6 +557,14 @@ int main(int argc, char** argv) {
                 if (i + 1 < a.dwordsC) o << ",";
             }
         }
+    }
+    if (!a.dumpB.empty()) {
+        // Raw dump of B after the last launch (for kernel files that keep
+        // state there, e.g. the side map and its diagnostics).
+        std::vector<uint32_t> hB(a.dwordsB);
+        ck(dyn::p_cuMemcpyDtoH(hB.data(), dB, sizeB), "cuMemcpyDtoH B");
+        std::ofstream o(a.dumpB, std::ios::binary);
+        o.write(reinterpret_cast<const char*>(hB.data()), (std::streamsize)sizeB);
     }
     long firstDiff = -1;
     if (!a.referenceC.empty()) {
