@@ -88,7 +88,7 @@ constexpr int kMaxSm = 256;
 //   QRC_LOAD_KIND  0 ld.global.v4, 1 ld.global.nc.L1::no_allocate.L2::256B.v4,
 //                  2 as 1 plus L2::evict_first, 3 256-bit ld.global.nc.v8
 #ifndef QRC_MAX_GRAB
-#define QRC_MAX_GRAB 8
+#define QRC_MAX_GRAB 1
 #endif
 #ifndef QRC_LOAD_KIND
 #define QRC_LOAD_KIND 1
@@ -119,6 +119,12 @@ constexpr int kMaxSm = 256;
 //                  reduce_run); 0: every pair through the side queues
 #ifndef QRC_SHARES
 #define QRC_SHARES 1
+#endif
+//   QRC_STATIC_EIGHTHS  eighths of the pairs covered by static shares; the
+//                  rest goes through the side queues, which absorb SMs that
+//                  run slower than their share assumes
+#ifndef QRC_STATIC_EIGHTHS
+#define QRC_STATIC_EIGHTHS 7
 #endif
 //   QRC_ACROSS     1: a warp takes its next 8 chunks together and loads slice k
 //                  of all 8 before slice k+1 (8 chunks in flight, one 512-byte
@@ -736,6 +742,14 @@ struct SideWalk : ChunkMap {
         p1 = st + sz < nq ? st + sz : nq;
         request(lane, st, sz);
     }
+    // Takes over a first request issued before the walk was built: lane 0's
+    // `st` is the counter value returned for a grab of `sz` positions.
+    QRC_MEMBER void begin_with(qrc_u64 st, qrc_u32 sz) {
+        p = p1 = 0;
+        nstart = st;
+        nsize = sz;
+        pending = nq > 0;
+    }
     // First request; does not wait for the reply.
     QRC_MEMBER void begin(int lane) {
         p = p1 = 0;
@@ -952,6 +966,7 @@ QRC_DEV qrc_u32 block_max(qrc_u32 bits) {
 // through 8*G adjacent pairs while the M SMs of a side sweep one window.
 // Requires 4 KiB chunks (one 16-byte load per thread covers a chunk).
 struct Shares {
+    qrc_u64 R;          // pairs [0, R) are shared out statically
     qrc_u32 M;
     bool on;
 };
@@ -960,7 +975,7 @@ template <class Op>
 QRC_DEV typename Op::Acc read_share(typename Op::Acc acc, const ChunkMap& w, const Shares& sh, int s, int k
                                     QRC_CS_PARAM) {
     const int G = blockDim.x >> 8, g = threadIdx.x >> 8, t = threadIdx.x & 255;
-    const qrc_u64 groups = (qrc_u64)sh.M * G, npairs = w.npairs;
+    const qrc_u64 groups = (qrc_u64)sh.M * G, npairs = sh.R;
     qrc_u64 b = (qrc_u64)k * G + g;
     if ((w.lo & 0xFFFFull) == 0) {
         // Fast path: a block is 64 KiB aligned, so its 8 pairs share one page
@@ -1012,9 +1027,15 @@ QRC_DEV typename Op::Acc read_share(typename Op::Acc acc, const ChunkMap& w, con
 // Side-aware path (modes 0-2), register loads:
 //   * Static shares: discovery gave every SM its side s and a dense index k
 //     among the K_s SMs of that side.  With M = min(K_0, K_1), the CTA on SM
-//     (s, k < M) reads the side-s chunk of its share of every pair (see
-//     read_share); SMs with k >= M sit out, so both sides carry equal work per
-//     SM.  No atomics.  The CTA marks its share with a plain store.
+//     (s, k < M) reads the side-s chunk of its share of the first
+//     R = QRC_STATIC_EIGHTHS/8 of the pairs (see read_share).  No atomics.
+//     The CTA marks its share with a plain store.
+//   * The remaining pairs go through the side queues (SideWalk): every CTA,
+//     including those of SMs without a share, takes one-pair grabs there
+//     after its share, so SMs that run slower than the static split assumes
+//     (the spread across SMs reaches ~10 % on B200) are absorbed, and a side
+//     that runs out helps the other.  The first request is issued before the
+//     share is read.
 //   * A maximum does not change when an element is read twice, so two CTAs on
 //     one SM only cost time.  A share nobody marked (an SM that got no CTA,
 //     e.g. a grid smaller than the GPU) is read by the last CTA after the
@@ -1069,6 +1090,7 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, float* out, floa
             const qrc_u32 k0 = map[H_NSIDE0], k1 = map[H_NSIDE1];
             sh.M = k0 < k1 ? k0 : k1;
             sh.on = sh.M > 0 && sh.M <= 128;
+            sh.R = (cm.npairs * QRC_STATIC_EIGHTHS / 8) & ~7ull;   // whole 8-pair blocks
         }
         griddep_wait();                   // the scratch of the previous launch is reset
 #if QRC_TIMELINE
@@ -1079,11 +1101,27 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, float* out, floa
             map[O_TIMELINE + 1022] = __ldcg(&map[O_TIMELINE + 1023]);
 #endif
         if (sh.on) {
+            // First queue request goes out now; only its reply stays live
+            // while the share is read.
+            const qrc_u64 nq = cm.npairs - sh.R;
+            qrc_u32* queue0 = &map[cm.side ? H_QUEUE1 : H_QUEUE0];
+            qrc_u32 first = 0;
+            if (lane == 0 && nq) first = atomicAdd(queue0, 1u);
             const int own_k = cm.sm_index;
             if (own_k >= 0 && (qrc_u32)own_k < sh.M) {
                 if (threadIdx.x == 0) *(volatile qrc_u32*)&map[O_CLAIMS + 128 * cm.side + own_k] = 1u;
                 acc = read_share<Op>(acc, cm, sh, cm.side, own_k QRC_CS_ARG);
             }
+            SideWalk w;
+            w.setup(a, end, map, mode);
+            w.set_queued(sh.R);
+            w.begin_with(first, 1u);
+            const int n512 = (int)(w.C >> 9);
+            for (qrc_u64 chunk = w.next(lane); chunk; chunk = w.next(lane))
+                acc = chunk_warp<Op>(acc, chunk, n512, lane QRC_CS_ARG);
+#if QRC_TIMELINE
+            stolen = w.stolen;
+#endif
         } else {
             SideWalk w;
             w.setup(a, end, map, mode);
