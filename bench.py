@@ -48,6 +48,8 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--mode", default="side_aware", choices=["side_aware", "ignore_page_bits", "wrong_side", "stream"])
+    ap.add_argument("--sched", default="auto", choices=["auto", "static", "queue"],
+                    help="work schedule: by size, fixed per-SM shares, or per-side queues")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-ablation", action="store_true")
@@ -244,6 +246,7 @@ def run_ours(args):
     init_ms = 1e3 * (time.perf_counter() - t0)
     info = ctx.info
     ctx.mode = args.mode
+    ctx.schedule = args.sched
     ctx.set_overlap(not args.no_overlap)
     out = torch.zeros(1, dtype=torch.float32, device=dev)
 
@@ -409,6 +412,7 @@ def run_ours(args):
         "warmup": max(args.warmup, 3), "ms_per_step": round(ms_per_step, 5), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": workload, "n_per_gpu": n, "bytes_per_gpu": nbytes, "mode": args.mode,
+                   "schedule": args.sched,
                    "overlap": not args.no_overlap,
                    "launch": f"{info['num_sms_measured'] or ''} SMs x 1 CTA x 1024 threads",
                    "l2": L2_NOTE, "parallelism": "replicated shards" if world == 1 else f"shard{world}+nccl_max_allreduce"},

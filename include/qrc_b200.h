@@ -48,7 +48,10 @@ enum qrc_mode {
     QRC_MODE_SIDE_AWARE = 0,        /* each side reads the chunks homed on it */
     QRC_MODE_IGNORE_PAGE_BITS = 1,  /* FORCE_RANDOM_SIDE: page bits treated as 0 */
     QRC_MODE_WRONG_SIDE = 2,        /* FORCE_WRONG_SIDE: every chunk read across the die boundary */
-    QRC_MODE_STREAM = 3             /* plain grid-stride stream, no side logic */
+    QRC_MODE_STREAM = 3,            /* plain grid-stride stream, no side logic */
+    /* Work schedule, OR-ed into a side-aware mode (default: chosen by size). */
+    QRC_SCHED_STATIC = 0x10,        /* every SM reads a fixed share: no atomics */
+    QRC_SCHED_QUEUE = 0x20          /* warps take one-pair grabs from per-side queues */
 };
 
 /* Discovery status (qrc_side_info.status). */
@@ -102,7 +105,8 @@ int qrc_ctx_destroy(qrc_ctx* ctx);
  * (tests/side_aware.cu:95-197). */
 int qrc_ctx_get_info(const qrc_ctx* ctx, qrc_side_info* info);
 
-/* Select the read mode (qrc_mode) for later reductions on this context.
+/* Select the read mode (qrc_mode, optionally OR-ed with a QRC_SCHED_* bit)
+ * for later reductions on this context.
  * Replaces the compile-time FORCE_RANDOM_SIDE / FORCE_WRONG_SIDE defines
  * (tests/side_aware.cu:19-20). */
 int qrc_ctx_set_mode(qrc_ctx* ctx, int mode);

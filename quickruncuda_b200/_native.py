@@ -32,6 +32,10 @@ MODE_SIDE_AWARE = 0
 MODE_IGNORE_PAGE_BITS = 1
 MODE_WRONG_SIDE = 2
 MODE_STREAM = 3
+SCHED_AUTO = 0x00
+SCHED_STATIC = 0x10
+SCHED_QUEUE = 0x20
+SCHED_NAMES = {"auto": SCHED_AUTO, "static": SCHED_STATIC, "queue": SCHED_QUEUE}
 MODE_NAMES = {"side_aware": MODE_SIDE_AWARE, "ignore_page_bits": MODE_IGNORE_PAGE_BITS,
               "random_side": MODE_IGNORE_PAGE_BITS, "wrong_side": MODE_WRONG_SIDE,
               "stream": MODE_STREAM}

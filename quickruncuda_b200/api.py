@@ -68,6 +68,7 @@ class SideAwareContext:
         self._h = h
         self.base, self.nbytes = base, size
         self._mode = nat.MODE_SIDE_AWARE
+        self._sched = nat.SCHED_AUTO
 
     # -- lifetime ----------------------------------------------------------
     def close(self) -> None:
@@ -112,9 +113,25 @@ class SideAwareContext:
 
     @mode.setter
     def mode(self, m) -> None:
-        m = nat.MODE_NAMES[m] if isinstance(m, str) else int(m)
+        """A name keeps the current schedule; an int (a qrc_mode, optionally
+        OR-ed with a schedule bit) sets both."""
+        m = nat.MODE_NAMES[m] | self._sched if isinstance(m, str) else int(m)
         nat.check(self.lib, "qrc_ctx_set_mode", self.lib.qrc_ctx_set_mode(self.handle, m))
-        self._mode = m
+        self._mode = m & 0xF
+        self._sched = m & ~0xF
+
+    @property
+    def schedule(self) -> str:
+        return {v: k for k, v in nat.SCHED_NAMES.items()}[self._sched]
+
+    @schedule.setter
+    def schedule(self, name: str) -> None:
+        """'auto' (by size), 'static' (fixed per-SM shares) or 'queue'
+        (one-pair grabs from per-side queues)."""
+        sched = nat.SCHED_NAMES[name]
+        nat.check(self.lib, "qrc_ctx_set_mode",
+                  self.lib.qrc_ctx_set_mode(self.handle, self._mode | sched))
+        self._sched = sched
 
     def set_launch(self, blocks_per_sm: int, threads: int) -> None:
         nat.check(self.lib, "qrc_ctx_set_launch",

@@ -19,7 +19,9 @@
 //   arg0     number of floats (`-0`)
 //   arg1     read mode (`-1`): 0 side-aware, 1 page bits ignored (the
 //            reference's FORCE_RANDOM_SIDE ablation), 2 every chunk read from
-//            the far side (FORCE_WRONG_SIDE), 3 side-agnostic grid-stride stream.
+//            the far side (FORCE_WRONG_SIDE), 3 side-agnostic grid-stride stream;
+//            plus 16 to force static shares or 32 to force the side queues
+//            (default: chosen by size).
 //            `-H '#define FORCE_RANDOM_SIDE'` / FORCE_WRONG_SIDE also work.
 //
 // How B200 is modelled (the reference's model, side_aware.cu:8-12, re-measured
@@ -124,7 +126,12 @@ constexpr int kMaxSm = 256;
 //                  rest goes through the side queues, which absorb SMs that
 //                  run slower than their share assumes
 #ifndef QRC_STATIC_EIGHTHS
-#define QRC_STATIC_EIGHTHS 7
+#define QRC_STATIC_EIGHTHS 8
+#endif
+//   QRC_STATIC_MAX_PAIRS  automatic schedule: static shares up to this many
+//                  8 KiB pairs, side queues above
+#ifndef QRC_STATIC_MAX_PAIRS
+#define QRC_STATIC_MAX_PAIRS 196608
 #endif
 //   QRC_ACROSS     1: a warp takes its next 8 chunks together and loads slice k
 //                  of all 8 before slice k+1 (8 chunks in flight, one 512-byte
@@ -173,6 +180,9 @@ enum : qrc_u32 {
 };
 
 enum : qrc_u32 { MODE_SIDE_AWARE = 0, MODE_IGNORE_PAGE_BITS = 1, MODE_WRONG_SIDE = 2, MODE_STREAM = 3 };
+// Schedule bits, OR-ed into the mode: automatic by size, static shares, or
+// side queues (see reduce_run).
+enum : qrc_u32 { SCHED_AUTO = 0x00, SCHED_STATIC = 0x10, SCHED_QUEUE = 0x20, SCHED_MASK = 0x30 };
 
 QRC_DEV qrc_u32 smid() {
     qrc_u32 r;
@@ -1048,6 +1058,8 @@ QRC_DEV typename Op::Acc read_share(typename Op::Acc acc, const ChunkMap& w, con
 // Mode 3: side-agnostic grid-stride stream.
 template <class Op>
 QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, float* out, float* scale_out, qrc_u32 mode) {
+    const qrc_u32 sched = mode & SCHED_MASK;
+    mode &= ~SCHED_MASK;
     const qrc_u64 a = (qrc_u64)A, bytes = n * (qrc_u64)Op::kElem, end = a + bytes;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, W = blockDim.x >> 5;
     typename Op::Acc acc = Op::zero();
@@ -1085,12 +1097,14 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, float* out, floa
         lo = cm.lo; hi = cm.hi;
         const int S = bulk_slots_per_warp(dynamic_smem_size(), W);
         sh.on = QRC_SHARES && cm.aware && S < 2 && cm.C == 4096 && (blockDim.x & 255) == 0 &&
-                (blockDim.x == 1024 || dynamic_smem_size() > 116u * 1024u);
+                (blockDim.x == 1024 || dynamic_smem_size() > 116u * 1024u) && sched != SCHED_QUEUE &&
+                (sched == SCHED_STATIC || cm.npairs <= (qrc_u64)QRC_STATIC_MAX_PAIRS);
         if (sh.on) {
             const qrc_u32 k0 = map[H_NSIDE0], k1 = map[H_NSIDE1];
             sh.M = k0 < k1 ? k0 : k1;
             sh.on = sh.M > 0 && sh.M <= 128;
-            sh.R = (cm.npairs * QRC_STATIC_EIGHTHS / 8) & ~7ull;   // whole 8-pair blocks
+            sh.R = QRC_STATIC_EIGHTHS >= 8 ? cm.npairs
+                                           : (cm.npairs * QRC_STATIC_EIGHTHS / 8) & ~7ull;   // whole 8-pair blocks
         }
         griddep_wait();                   // the scratch of the previous launch is reset
 #if QRC_TIMELINE
@@ -1280,9 +1294,9 @@ extern "C" __global__ void __launch_bounds__(1024, 1)
 kernel(float* A, unsigned int* side_map, float* C, int num_dwords, int mode, int arg2) {
     (void)arg2;
 #if defined(FORCE_WRONG_SIDE)
-    mode = qrc::MODE_WRONG_SIDE;
+    mode = (mode & qrc::SCHED_MASK) | qrc::MODE_WRONG_SIDE;
 #elif defined(FORCE_RANDOM_SIDE)
-    mode = qrc::MODE_IGNORE_PAGE_BITS;
+    mode = (mode & qrc::SCHED_MASK) | qrc::MODE_IGNORE_PAGE_BITS;
 #endif
     qrc::reduce_run<qrc::OpAbsF32>(A, num_dwords > 0 ? (qrc_u64)num_dwords : 0ull, side_map, C, nullptr,
                                    (qrc_u32)mode);
