@@ -981,27 +981,37 @@ struct Shares {
     bool on;
 };
 
+// Page-bit word of 8-pair block b when the share fast path (64 KiB aligned
+// body) reads it, else 0.  Page bits are written only by discovery, so this
+// load may go out before the wait on the previous grid.
+QRC_DEV qrc_u32 block_page_word(const ChunkMap& w, const Shares& sh, qrc_u64 b) {
+    if (!w.use_page_bits || (w.lo & 0xFFFFull) != 0 || (b + 1) * 8 > sh.R) return 0u;
+    const qrc_u64 pg = (w.lo + (b << 16) - w.page_base) >> 21;
+    return w.page_bits[pg >> 5];
+}
+QRC_DEV qrc_u32 share_first_page_word(const ChunkMap& w, const Shares& sh, int k) {
+    return block_page_word(w, sh, (qrc_u64)k * (blockDim.x >> 8) + (threadIdx.x >> 8));
+}
+
+// `pw` is share_first_page_word(w, sh, k).
 template <class Op>
-QRC_DEV typename Op::Acc read_share(typename Op::Acc acc, const ChunkMap& w, const Shares& sh, int s, int k
-                                    QRC_CS_PARAM) {
+QRC_DEV typename Op::Acc read_share(typename Op::Acc acc, const ChunkMap& w, const Shares& sh, int s, int k,
+                                    qrc_u32 pw QRC_CS_PARAM) {
     const int G = blockDim.x >> 8, g = threadIdx.x >> 8, t = threadIdx.x & 255;
     const qrc_u64 groups = (qrc_u64)sh.M * G, npairs = sh.R;
     qrc_u64 b = (qrc_u64)k * G + g;
     if ((w.lo & 0xFFFFull) == 0) {
         // Fast path: a block is 64 KiB aligned, so its 8 pairs share one page
         // bit, and pair j's masked-address parity is the block's XOR bit j of
-        // `pat` (address bits 13-15 are j).  One page-bit load and one popc
-        // per block.
+        // `pat` (address bits 13-15 are j).  One popc per block; the page-bit
+        // word of the next block is loaded with this block's data.
         qrc_u32 pat = 0;
         #pragma unroll
         for (int j = 0; j < 8; j++) pat |= (qrc_u32)parity64(((qrc_u64)j << 13) & w.mask) << j;
         for (; (b + 1) * 8 <= npairs; b += groups) {
             const qrc_u64 base = w.lo + (b << 16);
-            int pbit = 0;
-            if (w.use_page_bits) {
-                const qrc_u64 pg = (base - w.page_base) >> 21;
-                pbit = (w.page_bits[pg >> 5] >> (pg & 31)) & 1;
-            }
+            const int pbit = (int)(pw >> (((base - w.page_base) >> 21) & 31)) & 1;
+            pw = block_page_word(w, sh, b + groups);
             // chunk j is the second half when its first half is homed off side s
             const qrc_u32 second = (qrc_u32)(parity64(base & w.mask) ^ pbit ^ w.flip ^ s) ? ~pat : pat;
             const qrc_u64 row = base + 16ull * t;
@@ -1106,6 +1116,9 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, float* out, floa
             sh.R = QRC_STATIC_EIGHTHS >= 8 ? cm.npairs
                                            : (cm.npairs * QRC_STATIC_EIGHTHS / 8) & ~7ull;   // whole 8-pair blocks
         }
+        const int own_k = cm.sm_index;
+        const bool own_share = sh.on && own_k >= 0 && (qrc_u32)own_k < sh.M;
+        const qrc_u32 pw0 = own_share ? share_first_page_word(cm, sh, own_k) : 0u;
         griddep_wait();                   // the scratch of the previous launch is reset
 #if QRC_TIMELINE
         qrc_u64 t_start;
@@ -1121,21 +1134,22 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, float* out, floa
             qrc_u32* queue0 = &map[cm.side ? H_QUEUE1 : H_QUEUE0];
             qrc_u32 first = 0;
             if (lane == 0 && nq) first = atomicAdd(queue0, 1u);
-            const int own_k = cm.sm_index;
-            if (own_k >= 0 && (qrc_u32)own_k < sh.M) {
+            if (own_share) {
                 if (threadIdx.x == 0) *(volatile qrc_u32*)&map[O_CLAIMS + 128 * cm.side + own_k] = 1u;
-                acc = read_share<Op>(acc, cm, sh, cm.side, own_k QRC_CS_ARG);
+                acc = read_share<Op>(acc, cm, sh, cm.side, own_k, pw0 QRC_CS_ARG);
             }
-            SideWalk w;
-            w.setup(a, end, map, mode);
-            w.set_queued(sh.R);
-            w.begin_with(first, 1u);
-            const int n512 = (int)(w.C >> 9);
-            for (qrc_u64 chunk = w.next(lane); chunk; chunk = w.next(lane))
-                acc = chunk_warp<Op>(acc, chunk, n512, lane QRC_CS_ARG);
+            if (nq) {
+                SideWalk w;
+                w.setup(a, end, map, mode);
+                w.set_queued(sh.R);
+                w.begin_with(first, 1u);
+                const int n512 = (int)(w.C >> 9);
+                for (qrc_u64 chunk = w.next(lane); chunk; chunk = w.next(lane))
+                    acc = chunk_warp<Op>(acc, chunk, n512, lane QRC_CS_ARG);
 #if QRC_TIMELINE
-            stolen = w.stolen;
+                stolen = w.stolen;
 #endif
+            }
         } else {
             SideWalk w;
             w.setup(a, end, map, mode);
@@ -1222,9 +1236,12 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, float* out, floa
     // ---- last CTA: unmarked shares, then publish ---------------------------
     // Thread 0 takes the accumulator while warp 0 checks the share marks, in
     // the same round trip; only a missing share costs more.
-    __shared__ qrc_u32 s_acc;
+    __shared__ qrc_u32 s_acc, s_wait_err;
     __shared__ int s_share;
-    if (threadIdx.x == 0) s_acc = atomicExch(&map[H_ACC], 0u);
+    if (threadIdx.x == 0) {
+        s_acc = atomicExch(&map[H_ACC], 0u);
+        s_wait_err = __ldcg(&map[H_WAIT_ERR]);
+    }
     typename Op::Acc acc2 = Op::zero();
     bool extra = false;
     if (sh.on) {
@@ -1252,7 +1269,8 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, float* out, floa
             extra = true;
             ChunkMap cm;                      // only when a share was missed
             cm.setup(a, end, map, mode);
-            acc2 = read_share<Op>(acc2, cm, sh, pick >> 7, pick & 127 QRC_CS_ARG);
+            acc2 = read_share<Op>(acc2, cm, sh, pick >> 7, pick & 127, share_first_page_word(cm, sh, pick & 127)
+                                  QRC_CS_ARG);
         }
         for (int i = threadIdx.x; i < 256; i += blockDim.x) map[O_CLAIMS + i] = 0u;
 #ifdef QRC_CHECKED
@@ -1267,7 +1285,7 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, float* out, floa
         r = r > v2 ? r : v2;
         map[H_QUEUE0] = 0u;
         map[H_QUEUE1] = 0u;
-        if (map[H_WAIT_ERR]) r = 0x7FFFFFFFu;   // a bounded wait gave up: no valid maximum
+        if (s_wait_err) r = 0x7FFFFFFFu;        // a bounded wait gave up: no valid maximum
         out[0] = __uint_as_float(r);
 #if QRC_TIMELINE
         qrc_u64 t_fin;
