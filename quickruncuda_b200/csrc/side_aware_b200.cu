@@ -88,7 +88,8 @@ constexpr int kMaxSm = 256;
 //   QRC_MAX_GRAB   most pairs a warp takes per queue atomic (guided: grabs
 //                  shrink to 1 pair as its side's queue empties)
 //   QRC_LOAD_KIND  0 ld.global.v4, 1 ld.global.nc.L1::no_allocate.L2::256B.v4,
-//                  2 as 1 plus L2::evict_first, 3 256-bit ld.global.nc.v8
+//                  2 as 1 plus L2::evict_first, 3 256-bit ld.global.nc.v8,
+//                  4 ld.global.nc.L1::no_allocate.v4 (no L2 prefetch size)
 #ifndef QRC_MAX_GRAB
 #define QRC_MAX_GRAB 1
 #endif
@@ -130,6 +131,12 @@ constexpr int kMaxSm = 256;
 #endif
 //   QRC_STATIC_MAX_PAIRS  automatic schedule: static shares up to this many
 //                  8 KiB pairs, side queues above
+//   QRC_PLAIN_MAX_BYTES  static shares of inputs up to this size are read
+//                  with plain ld.global.v4 (flavour 0), larger ones with
+//                  QRC_LOAD_KIND
+#ifndef QRC_PLAIN_MAX_BYTES
+#define QRC_PLAIN_MAX_BYTES (96ull << 20)
+#endif
 #ifndef QRC_STATIC_MAX_PAIRS
 #define QRC_STATIC_MAX_PAIRS 196608
 #endif
@@ -482,21 +489,26 @@ QRC_DEV qrc_u32 absmax_step_bf16x2(qrc_u32 acc, qrc_u32 x) {
 }
 
 // Streaming 16-byte load (flavour chosen by QRC_LOAD_KIND).
-QRC_DEV uint4 ld_stream16(qrc_u64 addr) {
+template <int Kind>
+QRC_DEV uint4 ld16(qrc_u64 addr) {
     uint4 v;
-#if QRC_LOAD_KIND == 0
-    asm volatile("ld.global.v4.u32 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(addr));
-#elif QRC_LOAD_KIND == 2
-    asm volatile("{\n\t.reg .b64 pol;\n\tcreatepolicy.fractional.L2::evict_first.b64 pol, 1.0;\n\t"
-                 "ld.global.nc.L1::no_allocate.L2::cache_hint.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4], pol;\n\t}"
-                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(addr));
-#else
-    asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(addr));
-#endif
+    if constexpr (Kind == 0) {
+        asm volatile("ld.global.v4.u32 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(addr));
+    } else if constexpr (Kind == 2) {
+        asm volatile("{\n\t.reg .b64 pol;\n\tcreatepolicy.fractional.L2::evict_first.b64 pol, 1.0;\n\t"
+                     "ld.global.nc.L1::no_allocate.L2::cache_hint.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4], pol;\n\t}"
+                     : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(addr));
+    } else if constexpr (Kind == 4) {
+        asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(addr));
+    } else {
+        asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(addr));
+    }
     return v;
 }
+QRC_DEV uint4 ld_stream16(qrc_u64 addr) { return ld16<QRC_LOAD_KIND>(addr); }
 
 #if QRC_LOAD_KIND == 3
 // 32-byte load (sm_100 256-bit global loads), as two uint4.
@@ -583,10 +595,10 @@ QRC_DEV typename Op::Acc edge_warp(typename Op::Acc acc, qrc_u64 x0, qrc_u64 x1,
 // Reads one C-byte chunk (C >= 512) with a warp: lane l reads 16 bytes at
 // l*16 + k*512 for k < C/512 (or, with 256-bit loads, 32 bytes at
 // l*32 + k*1024); eight 16-byte loads' worth are kept in flight per lane.
-template <class Op>
+template <class Op, int Kind = QRC_LOAD_KIND>
 QRC_DEV typename Op::Acc chunk_warp(typename Op::Acc acc, qrc_u64 chunk, int n512, int lane QRC_CS_PARAM) {
 #if QRC_LOAD_KIND == 3 && !defined(QRC_CHECKED)
-    if (n512 >= 2) {
+    if (Kind == 3 && n512 >= 2) {
         const qrc_u64 base = chunk + 32ull * lane;
         const int n1k = n512 >> 1;
         for (int k = 0; k < n1k; k += 4) {
@@ -609,7 +621,7 @@ QRC_DEV typename Op::Acc chunk_warp(typename Op::Acc acc, qrc_u64 chunk, int n51
         for (int u = 0; u < 8; u++) {
             v[u] = make_uint4(0u, 0u, 0u, 0u);
             const qrc_u64 x = base + 512ull * (k + u);
-            if (k + u < n512) { QRC_CHECK(x, 16) v[u] = ld_stream16(x); }
+            if (k + u < n512) { QRC_CHECK(x, 16) v[u] = ld16<Kind>(x); }
         }
         #pragma unroll
         for (int u = 0; u < 8; u++) acc = Op::step16(acc, v[u]);
@@ -994,7 +1006,7 @@ QRC_DEV qrc_u32 share_first_page_word(const ChunkMap& w, const Shares& sh, int k
 }
 
 // `pw` is share_first_page_word(w, sh, k).
-template <class Op>
+template <class Op, int Kind = QRC_LOAD_KIND>
 QRC_DEV typename Op::Acc read_share(typename Op::Acc acc, const ChunkMap& w, const Shares& sh, int s, int k,
                                     qrc_u32 pw QRC_CS_PARAM) {
     const int G = blockDim.x >> 8, g = threadIdx.x >> 8, t = threadIdx.x & 255;
@@ -1019,7 +1031,7 @@ QRC_DEV typename Op::Acc read_share(typename Op::Acc acc, const ChunkMap& w, con
             #pragma unroll
             for (int j = 0; j < 8; j++) {
                 const qrc_u64 x = row + ((qrc_u64)j << 13) + ((qrc_u64)((second >> j) & 1u) << 12);
-                QRC_CHECK(x, 16) v[j] = ld_stream16(x);
+                QRC_CHECK(x, 16) v[j] = ld16<Kind>(x);
             }
             #pragma unroll
             for (int j = 0; j < 8; j++) acc = Op::step16(acc, v[j]);
@@ -1033,7 +1045,7 @@ QRC_DEV typename Op::Acc read_share(typename Op::Acc acc, const ChunkMap& w, con
             const qrc_u64 pair = b * 8 + j;
             if (pair < npairs) {
                 const qrc_u64 x = w.chunk_of(pair, s) + 16ull * t;
-                QRC_CHECK(x, 16) v[j] = ld_stream16(x);
+                QRC_CHECK(x, 16) v[j] = ld16<Kind>(x);
             }
         }
         #pragma unroll
@@ -1071,6 +1083,9 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, float* out, floa
     const qrc_u32 sched = mode & SCHED_MASK;
     mode &= ~SCHED_MASK;
     const qrc_u64 a = (qrc_u64)A, bytes = n * (qrc_u64)Op::kElem, end = a + bytes;
+    // Inputs that can stay in L2 between launches are read with plain loads,
+    // which kept them resident where the non-coherent path did not.
+    const bool plain = bytes <= (qrc_u64)QRC_PLAIN_MAX_BYTES;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, W = blockDim.x >> 5;
     typename Op::Acc acc = Op::zero();
 #ifdef QRC_CHECKED
@@ -1136,7 +1151,8 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, float* out, floa
             if (lane == 0 && nq) first = atomicAdd(queue0, 1u);
             if (own_share) {
                 if (threadIdx.x == 0) *(volatile qrc_u32*)&map[O_CLAIMS + 128 * cm.side + own_k] = 1u;
-                acc = read_share<Op>(acc, cm, sh, cm.side, own_k, pw0 QRC_CS_ARG);
+                acc = plain ? read_share<Op, 0>(acc, cm, sh, cm.side, own_k, pw0 QRC_CS_ARG)
+                            : read_share<Op>(acc, cm, sh, cm.side, own_k, pw0 QRC_CS_ARG);
             }
             if (nq) {
                 SideWalk w;
