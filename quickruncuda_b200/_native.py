@@ -35,7 +35,8 @@ MODE_STREAM = 3
 SCHED_AUTO = 0x00
 SCHED_STATIC = 0x10
 SCHED_QUEUE = 0x20
-SCHED_NAMES = {"auto": SCHED_AUTO, "static": SCHED_STATIC, "queue": SCHED_QUEUE}
+SCHED_BALANCED = 0x30
+SCHED_NAMES = {"auto": SCHED_AUTO, "static": SCHED_STATIC, "queue": SCHED_QUEUE, "balanced": SCHED_BALANCED}
 MODE_NAMES = {"side_aware": MODE_SIDE_AWARE, "ignore_page_bits": MODE_IGNORE_PAGE_BITS,
               "random_side": MODE_IGNORE_PAGE_BITS, "wrong_side": MODE_WRONG_SIDE,
               "stream": MODE_STREAM}

@@ -308,7 +308,8 @@ QRC_API int qrc_ctx_get_info(const qrc_ctx* c, qrc_side_info* info) {
 QRC_API int qrc_ctx_set_mode(qrc_ctx* c, int mode) {
     const int read_mode = mode & 0xF, sched = mode & ~0xF;
     if (!c || read_mode < QRC_MODE_SIDE_AWARE || read_mode > QRC_MODE_STREAM ||
-        (sched != 0 && sched != QRC_SCHED_STATIC && sched != QRC_SCHED_QUEUE)) return QRC_ERR_INVALID;
+        (sched != 0 && sched != QRC_SCHED_STATIC && sched != QRC_SCHED_QUEUE && sched != QRC_SCHED_BALANCED))
+        return QRC_ERR_INVALID;
     c->mode = mode;
     if (c->stage_ctx) c->stage_ctx->mode = mode;
     return QRC_OK;

@@ -20,8 +20,8 @@
 //   arg1     read mode (`-1`): 0 side-aware, 1 page bits ignored (the
 //            reference's FORCE_RANDOM_SIDE ablation), 2 every chunk read from
 //            the far side (FORCE_WRONG_SIDE), 3 side-agnostic grid-stride stream;
-//            plus 16 to force static shares or 32 to force the side queues
-//            (default: chosen by size).
+//            plus 16 to force static shares, 32 the side queues, 48 static
+//            shares with a queued tail (default: chosen by size).
 //            `-H '#define FORCE_RANDOM_SIDE'` / FORCE_WRONG_SIDE also work.
 //
 // How B200 is modelled (the reference's model, side_aware.cu:8-12, re-measured
@@ -123,14 +123,15 @@ constexpr int kMaxSm = 256;
 #ifndef QRC_SHARES
 #define QRC_SHARES 1
 #endif
-//   QRC_STATIC_EIGHTHS  eighths of the pairs covered by static shares; the
-//                  rest goes through the side queues, which absorb SMs that
-//                  run slower than their share assumes
+//   QRC_STATIC_EIGHTHS  balanced schedule: eighths of the pairs covered by
+//                  static shares; the rest is claimed block by block from the
+//                  side queues, which absorbs SMs that run slower than their
+//                  share assumes
 #ifndef QRC_STATIC_EIGHTHS
-#define QRC_STATIC_EIGHTHS 8
+#define QRC_STATIC_EIGHTHS 5
 #endif
-//   QRC_STATIC_MAX_PAIRS  automatic schedule: static shares up to this many
-//                  8 KiB pairs, side queues above
+//   QRC_STATIC_MAX_PAIRS  automatic schedule: static shares alone up to this
+//                  many 8 KiB pairs, the balanced schedule above
 //   QRC_PLAIN_MAX_BYTES  static shares of inputs up to this size are read
 //                  with plain ld.global.v4 (flavour 0), larger ones with
 //                  QRC_LOAD_KIND
@@ -138,7 +139,7 @@ constexpr int kMaxSm = 256;
 #define QRC_PLAIN_MAX_BYTES (96ull << 20)
 #endif
 #ifndef QRC_STATIC_MAX_PAIRS
-#define QRC_STATIC_MAX_PAIRS 196608
+#define QRC_STATIC_MAX_PAIRS 32768
 #endif
 //   QRC_ACROSS     1: a warp takes its next 8 chunks together and loads slice k
 //                  of all 8 before slice k+1 (8 chunks in flight, one 512-byte
@@ -187,9 +188,10 @@ enum : qrc_u32 {
 };
 
 enum : qrc_u32 { MODE_SIDE_AWARE = 0, MODE_IGNORE_PAGE_BITS = 1, MODE_WRONG_SIDE = 2, MODE_STREAM = 3 };
-// Schedule bits, OR-ed into the mode: automatic by size, static shares, or
-// side queues (see reduce_run).
-enum : qrc_u32 { SCHED_AUTO = 0x00, SCHED_STATIC = 0x10, SCHED_QUEUE = 0x20, SCHED_MASK = 0x30 };
+// Schedule bits, OR-ed into the mode: automatic by size, static shares, side
+// queues, or static shares with a queued tail (see reduce_run).
+enum : qrc_u32 { SCHED_AUTO = 0x00, SCHED_STATIC = 0x10, SCHED_QUEUE = 0x20, SCHED_BALANCED = 0x30,
+                 SCHED_MASK = 0x30 };
 
 QRC_DEV qrc_u32 smid() {
     qrc_u32 r;
@@ -979,18 +981,20 @@ QRC_DEV qrc_u32 block_max(qrc_u32 bits) {
     return s_res;
 }
 
-// Static shares (see reduce_run).  M = min(K_0, K_1) SMs per side take part.
+// Static shares (see reduce_run).  All K_s SMs of side s take part; the two
+// sides are not paired, each covers its own chunk of every pair.
 // A 256-thread group reads the side-s chunks of 8 consecutive pairs at once:
 // thread t loads bytes 16t..16t+15 of each of the 8 chunks (eight 16-byte
 // loads in flight, all addresses computed on the spot).  Block b of 8 pairs
-// belongs to group b mod (M * G) of the side, G = groups per CTA, and group g
+// belongs to group b mod (K_s * G) of side s, G = groups per CTA, and group g
 // of the CTA on the SM with index k is group k * G + g, so each SM steps
-// through 8*G adjacent pairs while the M SMs of a side sweep one window.
+// through 8*G adjacent pairs while the K_s SMs of a side sweep one window.
 // Requires 4 KiB chunks (one 16-byte load per thread covers a chunk).
 struct Shares {
     qrc_u64 R;          // pairs [0, R) are shared out statically
-    qrc_u32 M;
+    qrc_u32 K0, K1;     // SMs per side
     bool on;
+    QRC_MEMBER qrc_u32 sms(int s) const { return s ? K1 : K0; }
 };
 
 // Page-bit word of 8-pair block b when the share fast path (64 KiB aligned
@@ -1010,7 +1014,7 @@ template <class Op, int Kind = QRC_LOAD_KIND>
 QRC_DEV typename Op::Acc read_share(typename Op::Acc acc, const ChunkMap& w, const Shares& sh, int s, int k,
                                     qrc_u32 pw QRC_CS_PARAM) {
     const int G = blockDim.x >> 8, g = threadIdx.x >> 8, t = threadIdx.x & 255;
-    const qrc_u64 groups = (qrc_u64)sh.M * G, npairs = sh.R;
+    const qrc_u64 groups = (qrc_u64)sh.sms(s) * G, npairs = sh.R;
     qrc_u64 b = (qrc_u64)k * G + g;
     if ((w.lo & 0xFFFFull) == 0) {
         // Fast path: a block is 64 KiB aligned, so its 8 pairs share one page
@@ -1054,20 +1058,97 @@ QRC_DEV typename Op::Acc read_share(typename Op::Acc acc, const ChunkMap& w, con
     return acc;
 }
 
+QRC_DEV void group_bar(int g) {
+    asm volatile("bar.sync %0, 256;" :: "r"(1 + g) : "memory");
+}
+
+// Tail of the balanced schedule: pairs [R, npairs) in 8-pair blocks, taken one
+// block per claim from the side's queue by each 256-thread group (the group's
+// first thread claims, a named barrier hands the claim to the group).  The
+// next claim is in flight while the current block is read.  When its own
+// queue is empty, a group helps the other side (far reads).  `first` is the
+// group leader's first claim, issued before the static share was read.
+template <class Op, int Kind = QRC_LOAD_KIND>
+QRC_DEV typename Op::Acc read_tail(typename Op::Acc acc, const ChunkMap& w, qrc_u64 R, qrc_u32* map, int s,
+                                   qrc_u32 first QRC_CS_PARAM) {
+    __shared__ qrc_u32 s_claim[2][4];
+    const int g = threadIdx.x >> 8, t = threadIdx.x & 255;
+    const bool leader = t == 0;
+    const qrc_u64 nb = (w.npairs - R + 7) >> 3;
+    const bool fast = ((w.lo + (R << 13)) & 0xFFFFull) == 0;
+    qrc_u32 pat = 0;
+    #pragma unroll
+    for (int j = 0; j < 8; j++) pat |= (qrc_u32)parity64(((qrc_u64)j << 13) & w.mask) << j;
+    qrc_u32* queue = &map[s ? H_QUEUE1 : H_QUEUE0];
+    bool stealing = false;
+    int par = 0;
+    if (leader) s_claim[0][g] = first;
+    group_bar(g);
+    qrc_u32 cur = s_claim[0][g];
+    for (;;) {
+        qrc_u32 nxt = 0;
+        if (cur >= nb) {
+            if (stealing || !QRC_STEAL) break;
+            stealing = true;
+            s ^= 1;
+            queue = &map[s ? H_QUEUE1 : H_QUEUE0];
+            if (leader) nxt = atomicAdd(queue, 1u);
+        } else {
+            if (leader) nxt = atomicAdd(queue, 1u);
+            const qrc_u64 p0 = R + ((qrc_u64)cur << 3);
+            uint4 v[8];
+            if (fast && p0 + 8 <= w.npairs) {
+                const qrc_u64 base = w.lo + (p0 << 13);
+                int pbit = 0;
+                if (w.use_page_bits) {
+                    const qrc_u64 pg = (base - w.page_base) >> 21;
+                    pbit = (int)(w.page_bits[pg >> 5] >> (pg & 31)) & 1;
+                }
+                const qrc_u32 second = (qrc_u32)(parity64(base & w.mask) ^ pbit ^ w.flip ^ s) ? ~pat : pat;
+                const qrc_u64 row = base + 16ull * t;
+                #pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    const qrc_u64 x = row + ((qrc_u64)j << 13) + ((qrc_u64)((second >> j) & 1u) << 12);
+                    QRC_CHECK(x, 16) v[j] = ld16<Kind>(x);
+                }
+            } else {
+                #pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    v[j] = make_uint4(0u, 0u, 0u, 0u);
+                    const qrc_u64 pair = p0 + j;
+                    if (pair < w.npairs) {
+                        const qrc_u64 x = w.chunk_of(pair, s) + 16ull * t;
+                        QRC_CHECK(x, 16) v[j] = ld16<Kind>(x);
+                    }
+                }
+            }
+            #pragma unroll
+            for (int j = 0; j < 8; j++) acc = Op::step16(acc, v[j]);
+        }
+        // A slot is rewritten two barriers after it was read.
+        par ^= 1;
+        if (leader) s_claim[par][g] = nxt;
+        group_bar(g);
+        cur = s_claim[par][g];
+    }
+    return acc;
+}
+
 // The reduction over n elements at A (element type given by Op).
 //
 // Side-aware path (modes 0-2), register loads:
 //   * Static shares: discovery gave every SM its side s and a dense index k
-//     among the K_s SMs of that side.  With M = min(K_0, K_1), the CTA on SM
-//     (s, k < M) reads the side-s chunk of its share of the first
-//     R = QRC_STATIC_EIGHTHS/8 of the pairs (see read_share).  No atomics.
-//     The CTA marks its share with a plain store.
-//   * The remaining pairs go through the side queues (SideWalk): every CTA,
-//     including those of SMs without a share, takes one-pair grabs there
-//     after its share, so SMs that run slower than the static split assumes
-//     (the spread across SMs reaches ~10 % on B200) are absorbed, and a side
-//     that runs out helps the other.  The first request is issued before the
-//     share is read.
+//     among the K_s SMs of that side.  The CTA on SM (s, k) reads the side-s
+//     chunks of its share of pairs [0, R) (see read_share).  No atomics.  The
+//     CTA marks its share with a plain store.  R is every pair (static
+//     schedule), or 5/8 of them (balanced schedule, QRC_STATIC_EIGHTHS).
+//   * Balanced schedule: the pairs past R go in 8-pair blocks through the
+//     side queues, one block per claim by each 256-thread group (read_tail),
+//     so SMs that run slower than the static split assumes (the spread across
+//     SMs of one side reaches ~7 % on B200) are absorbed, and a side that
+//     runs out helps the other.  The first claim is issued before the share
+//     is read.
+//   * Queue schedule: no shares; warps take one-pair grabs (SideWalk).
 //   * A maximum does not change when an element is read twice, so two CTAs on
 //     one SM only cost time.  A share nobody marked (an SM that got no CTA,
 //     e.g. a grid smaller than the GPU) is read by the last CTA after the
@@ -1094,7 +1175,7 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, float* out, floa
     qrc_u64 lo, hi;   // body [lo, hi); edges [a, lo) and [hi, end)
     Shares sh;
     sh.on = false;
-    sh.M = 0;
+    sh.K0 = sh.K1 = 0;
 
     if (mode == MODE_STREAM) {
         // Side-agnostic grid-stride stream over the 16-byte aligned body.
@@ -1122,17 +1203,19 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, float* out, floa
         lo = cm.lo; hi = cm.hi;
         const int S = bulk_slots_per_warp(dynamic_smem_size(), W);
         sh.on = QRC_SHARES && cm.aware && S < 2 && cm.C == 4096 && (blockDim.x & 255) == 0 &&
-                (blockDim.x == 1024 || dynamic_smem_size() > 116u * 1024u) && sched != SCHED_QUEUE &&
-                (sched == SCHED_STATIC || cm.npairs <= (qrc_u64)QRC_STATIC_MAX_PAIRS);
+                blockDim.x <= 1024 && (blockDim.x == 1024 || dynamic_smem_size() > 116u * 1024u) &&
+                sched != SCHED_QUEUE;
         if (sh.on) {
             const qrc_u32 k0 = map[H_NSIDE0], k1 = map[H_NSIDE1];
-            sh.M = k0 < k1 ? k0 : k1;
-            sh.on = sh.M > 0 && sh.M <= 128;
-            sh.R = QRC_STATIC_EIGHTHS >= 8 ? cm.npairs
-                                           : (cm.npairs * QRC_STATIC_EIGHTHS / 8) & ~7ull;   // whole 8-pair blocks
+            sh.K0 = k0;
+            sh.K1 = k1;
+            sh.on = k0 > 0 && k1 > 0 && k0 <= 128 && k1 <= 128;
+            const bool tail = sched == SCHED_BALANCED ||
+                              (sched == SCHED_AUTO && cm.npairs > (qrc_u64)QRC_STATIC_MAX_PAIRS);
+            sh.R = tail ? (cm.npairs * QRC_STATIC_EIGHTHS / 8) & ~7ull : cm.npairs;   // whole 8-pair blocks
         }
         const int own_k = cm.sm_index;
-        const bool own_share = sh.on && own_k >= 0 && (qrc_u32)own_k < sh.M;
+        const bool own_share = sh.on && own_k >= 0 && (qrc_u32)own_k < sh.sms(cm.side);
         const qrc_u32 pw0 = own_share ? share_first_page_word(cm, sh, own_k) : 0u;
         griddep_wait();                   // the scratch of the previous launch is reset
 #if QRC_TIMELINE
@@ -1143,29 +1226,17 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, float* out, floa
             map[O_TIMELINE + 1022] = __ldcg(&map[O_TIMELINE + 1023]);
 #endif
         if (sh.on) {
-            // First queue request goes out now; only its reply stays live
+            // The tail's first claim goes out now; only its reply stays live
             // while the share is read.
-            const qrc_u64 nq = cm.npairs - sh.R;
-            qrc_u32* queue0 = &map[cm.side ? H_QUEUE1 : H_QUEUE0];
+            const bool tail = cm.npairs > sh.R;
             qrc_u32 first = 0;
-            if (lane == 0 && nq) first = atomicAdd(queue0, 1u);
+            if (tail && (threadIdx.x & 255) == 0) first = atomicAdd(&map[cm.side ? H_QUEUE1 : H_QUEUE0], 1u);
             if (own_share) {
                 if (threadIdx.x == 0) *(volatile qrc_u32*)&map[O_CLAIMS + 128 * cm.side + own_k] = 1u;
                 acc = plain ? read_share<Op, 0>(acc, cm, sh, cm.side, own_k, pw0 QRC_CS_ARG)
                             : read_share<Op>(acc, cm, sh, cm.side, own_k, pw0 QRC_CS_ARG);
             }
-            if (nq) {
-                SideWalk w;
-                w.setup(a, end, map, mode);
-                w.set_queued(sh.R);
-                w.begin_with(first, 1u);
-                const int n512 = (int)(w.C >> 9);
-                for (qrc_u64 chunk = w.next(lane); chunk; chunk = w.next(lane))
-                    acc = chunk_warp<Op>(acc, chunk, n512, lane QRC_CS_ARG);
-#if QRC_TIMELINE
-                stolen = w.stolen;
-#endif
-            }
+            if (tail) acc = read_tail<Op>(acc, cm, sh.R, map, cm.side, first QRC_CS_ARG);
         } else {
             SideWalk w;
             w.setup(a, end, map, mode);
@@ -1270,7 +1341,7 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, float* out, floa
                 #pragma unroll
                 for (int t = 7; t >= 0; t--) {
                     const int k = (32 * t + lane) & 127;
-                    const unsigned m = __ballot_sync(0xFFFFFFFFu, (qrc_u32)k < sh.M && mark[t] == 0u);
+                    const unsigned m = __ballot_sync(0xFFFFFFFFu, (qrc_u32)k < sh.sms(t >> 2) && mark[t] == 0u);
                     if (m) found = 32 * t + __ffs(m) - 1;
                 }
                 if (lane == 0) {

@@ -9,8 +9,9 @@ SIZES = [0, 1, 3, 4, 5, 1023, 4096, 8191, 8193, (1 << 19) - 1, (1 << 19) + 1,
          (2 * MIB) // 4 - 1, (2 * MIB) // 4, (2 * MIB) // 4 + 1, 3 * MIB + 7]
 OFFSETS = [0, 1, 3, 1021]          # floats into the context's buffer
 # read modes 0-3 with the schedule chosen by size (static shares at these
-# sizes), and forced schedules: 0x10 static shares, 0x20 per-side queues
-MODES = [0, 1, 2, 3, 0x20, 0x21, 0x22, 0x10]
+# sizes), and forced schedules: 0x10 static shares, 0x20 per-side queues,
+# 0x30 static shares with a queued tail
+MODES = [0, 1, 2, 3, 0x20, 0x21, 0x22, 0x10, 0x30, 0x31, 0x32]
 # (blocks per SM, threads per block, bulk slots per warp; 0 = register loads)
 SHAPES = [(1, 1024, 0), (2, 512, 0), (4, 256, 0), (1, 256, 6), (1, 512, 3), (1, 256, 2)]
 

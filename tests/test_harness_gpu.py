@@ -39,7 +39,7 @@ def harness_json(args, cwd):
 
 
 @pytest.mark.parametrize("arch", ["sm_100a", "sm_100"])
-@pytest.mark.parametrize("mode", [0, 1, 2, 3, 16, 32])
+@pytest.mark.parametrize("mode", [0, 1, 2, 3, 16, 32, 48])
 def test_kernel_file_under_our_harness_config1(tmp_path, oracle, arch, mode):
     n = 1048576
     res = harness_json(["-i", "-p", "-t", "1024", "-A", 4 * n, "-0", n, "-1", mode, "-C", 1, "-T", 5,

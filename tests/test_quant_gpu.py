@@ -75,7 +75,7 @@ def test_quant_config4_full_shape(cuda, qrc, oracle):
         assert np.float32(scale.item()) == so
         assert np.array_equal(q.cpu().numpy(), qo)
         # same again (scratch reset between launches) in the ablation modes
-        for mode in (1, 3, 0x20, 0x10):
+        for mode in (1, 3, 0x20, 0x10, 0x30):
             ctx.mode = mode
             q2, s2, _ = ctx.amax_quant_e4m3(x)
             assert np.float32(s2.item()) == so and torch.equal(q, q2)
