@@ -1,8 +1,9 @@
-"""Host model of the streaming kernel's work schedule (SideWalk in
-quickruncuda_b200/csrc/side_aware_b200.cu): the queue-position -> pair
-interleave must be a bijection for every size, and any split of the positions
-into grabs, on both sides, must read every byte exactly once whatever the side
-map says.  The device code itself is checked on the GPU by the checked build
+"""Host models of the streaming kernel's work schedules
+(quickruncuda_b200/csrc/side_aware_b200.cu).  Queue schedule (SideWalk): the
+queue-position -> pair interleave must be a bijection for every size, and any
+split of the positions into grabs, on both sides, must read every byte exactly
+once whatever the side map says.  Balanced schedule (read_share + read_tail):
+static blocks plus queued tail blocks, with stealing, cover every chunk once.  The device code itself is checked on the GPU by the checked build
 (tests/test_absmax_gpu.py::test_checked_build_every_byte_once_in_bounds)."""
 import numpy as np
 import pytest
@@ -67,3 +68,60 @@ def test_two_sides_cover_every_byte_once(oracle):
                     covered[2 * p + half] += 1
                 c += size
         assert np.all(covered == 1), trial
+
+
+def _balanced_cover(oracle, npairs, k0, k1, groups_per_cta, eighths, rng):
+    """Host model of the balanced schedule (reduce_run with static shares plus
+    read_tail): side s has K_s SMs of G groups; 8-pair block b < R/8 belongs
+    to group b mod (K_s * G); blocks past R are claimed from the side's queue
+    in any order, and a group whose queue is empty claims from the other
+    side's queue, reading that side's chunks."""
+    C = 4096
+    base = 1 << 30
+    mask = 0x1EF000
+    page_bits = rng.integers(0, 2, size=(npairs * 2 * C >> 21) + 2)
+    R = (npairs * eighths // 8) & ~7
+    covered = np.zeros(2 * npairs, dtype=np.int8)
+
+    def read_pair(p, side):
+        addr = base + p * 2 * C
+        half = oracle.pair_half(addr, mask, int(page_bits[(addr - base) >> 21]), side)
+        covered[2 * p + half] += 1
+
+    for side, k in ((0, k0), (1, k1)):
+        groups = k * groups_per_cta
+        for g in range(groups):
+            b = g
+            while b * 8 < R:
+                for p in range(b * 8, min(b * 8 + 8, R)):
+                    read_pair(p, side)
+                b += groups
+    nb = (npairs - R + 7) // 8
+    counters = [0, 0]
+    # claims in a random interleaving of groups from both sides, each group
+    # draining its own queue then the other one
+    agents = [(s, False) for s in (0, 1) for _ in range(3)]
+    while agents:
+        i = int(rng.integers(0, len(agents)))
+        side, stolen = agents[i]
+        q = side ^ 1 if stolen else side
+        c = counters[q]
+        counters[q] += 1
+        if c >= nb:
+            if stolen:
+                agents.pop(i)
+            else:
+                agents[i] = (side, True)
+            continue
+        for p in range(R + 8 * c, min(R + 8 * c + 8, npairs)):
+            read_pair(p, q)
+    return covered
+
+
+@pytest.mark.parametrize("npairs,k0,k1", [(1, 74, 74), (7, 70, 78), (100, 74, 74), (2047, 70, 78),
+                                          (5000, 76, 72), (12345, 1, 3)])
+@pytest.mark.parametrize("eighths", [5, 7, 8])
+def test_balanced_schedule_covers_every_chunk_once(oracle, npairs, k0, k1, eighths):
+    rng = np.random.default_rng(npairs + eighths)
+    covered = _balanced_cover(oracle, npairs, k0, k1, 4, eighths, rng)
+    assert np.all(covered == 1)
