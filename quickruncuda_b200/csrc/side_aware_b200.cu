@@ -55,11 +55,14 @@
 // Reduction (`kernel`) -- replaces side_aware.cu:257-395:
 //   * any grid and any block size that is a multiple of 32 (the reference
 //     needed exactly one 1024-thread block per SM, :266-269);
-//   * each CTA reads its SM's side from the map and its warps pull 8-pair
-//     "grabs" from that side's atomic work queue (one counter per side); for
-//     every pair a warp reads the C-byte half homed on its own side.  Both
-//     queues walk every pair, one half each, so every byte is read exactly once
-//     whatever the map says -- the map only decides locality, never coverage;
+//   * each CTA reads its SM's side from the map; for every pair it reads the
+//     C-byte half homed on its own side.  Both sides walk every pair, one half
+//     each, so every byte is read exactly once whatever the map says -- the
+//     map only decides locality, never coverage;
+//   * work goes out as static per-SM shares of 64 KiB blocks (inputs up to
+//     256 MiB), as static shares for 5/8 with the rest claimed block by
+//     block from a per-side queue (larger inputs), or as one-pair grabs from
+//     the per-side queues (launch shapes the shares cannot serve);
 //   * per element max(acc, |x|) with IEEE maxNum semantics written in PTX
 //     (NaN never wins, -0 -> +0, denormals kept even under -use_fast_math);
 //   * warp max with redux.sync.max.u32 on the (non-negative) float bits, one
