@@ -146,6 +146,25 @@ int qrc_ctx_set_overlap(qrc_ctx* ctx, int enable);
  * tests/side_aware.cu:257-395) with C[0] as the output. */
 int qrc_absmax_f32(const float* d_in, size_t n, float* d_out, qrc_ctx* ctx, void* stream);
 
+/* Reduction operators of qrc_reduce_f32. */
+enum qrc_op {
+    QRC_OP_ABSMAX = 0,              /* max |x|, float result (as qrc_absmax_f32) */
+    QRC_OP_MAX = 1,                 /* max x, float; NaN skipped, -0 below +0, empty gives -inf */
+    QRC_OP_MIN = 2,                 /* min x, float; NaN skipped, -0 below +0, empty gives +inf */
+    QRC_OP_SUM = 3,                 /* sum of x in double, double result */
+    QRC_OP_SUMSQ = 4                /* sum of x*x in double, double result */
+};
+
+/* The same side-aware walk with another reduction operator.  *d_out is one
+ * float for ABSMAX/MAX/MIN (bit-exact, deterministic) and one double for
+ * SUM/SUMSQ (d_out 8-byte aligned; every element is added exactly once, in
+ * an order that varies between launches, so the last bits may differ from
+ * one launch to the next).  Same context, alignment and stream rules as
+ * qrc_absmax_f32.
+ * Replaces: the reference's swappable reduction operator
+ * (tests/side_aware.cu:215-219), which needs an edit and a recompile there. */
+int qrc_reduce_f32(const float* d_in, size_t n, int op, void* d_out, qrc_ctx* ctx, void* stream);
+
 /* Same reduction for callers that cannot allocate device memory: a host
  * application that reserves all device memory up front and hands this code
  * only the buffers it works on, a process held to a fixed memory budget, or

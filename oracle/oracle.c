@@ -181,6 +181,59 @@ ORACLE_API float oracle_absmax_bf16(const uint16_t* x, size_t n) {
 }
 
 /* ------------------------------------------------------------------------- */
+/* The other reduction operators                                             */
+/* ------------------------------------------------------------------------- */
+
+/* The reference's operator is a swappable function (side_aware.cu:215-219,
+ * and the note at :11); the product offers max, min, sum and sum of squares
+ * besides absmax.  Their semantics, restated here:
+ *   max / min: NaN elements are skipped (maxNum / minNum); -0 orders below
+ *              +0; an empty or all-NaN input gives -inf (max) / +inf (min).
+ *   sum / sum of squares: every element once, in double; NaN and infinities
+ *              propagate as in IEEE addition.  The oracle sums with
+ *              Neumaier's compensated algorithm (Neumaier 1974), so its result
+ *              is within about one double rounding of the exact sum; it also
+ *              returns sum |term| so that tests can bound any summation order's
+ *              error by n * 2^-53 * sum |term|. */
+static inline uint32_t f32_key(float f) {
+    uint32_t b; memcpy(&b, &f, 4);
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+ORACLE_API float oracle_max_f32(const float* x, size_t n) {
+    float m = -INFINITY;
+    for (size_t i = 0; i < n; i++)
+        if (!isnan(x[i]) && f32_key(x[i]) > f32_key(m)) m = x[i];
+    return m;
+}
+
+ORACLE_API float oracle_min_f32(const float* x, size_t n) {
+    float m = INFINITY;
+    for (size_t i = 0; i < n; i++)
+        if (!isnan(x[i]) && f32_key(x[i]) < f32_key(m)) m = x[i];
+    return m;
+}
+
+static double neumaier(const float* x, size_t n, int square, double* abs_sum) {
+    double s = 0.0, c = 0.0, a = 0.0, plain = 0.0;
+    for (size_t i = 0; i < n; i++) {
+        const double v = square ? (double)x[i] * (double)x[i] : (double)x[i];   /* a float's square is exact in double */
+        const double t = s + v;
+        if (fabs(s) >= fabs(v)) c += (s - t) + v; else c += (v - t) + s;
+        s = t;
+        a += fabs(v);
+        plain += v;
+    }
+    if (abs_sum) *abs_sum = a;
+    /* Floats cannot overflow a double sum, so a non-finite plain sum means an
+     * infinity or NaN input: return IEEE addition's answer (inf, -inf or NaN). */
+    return isfinite(plain) ? s + c : plain;
+}
+
+ORACLE_API double oracle_sum_f32(const float* x, size_t n, double* abs_sum) { return neumaier(x, n, 0, abs_sum); }
+ORACLE_API double oracle_sumsq_f32(const float* x, size_t n, double* abs_sum) { return neumaier(x, n, 1, abs_sum); }
+
+/* ------------------------------------------------------------------------- */
 /* e4m3 (OCP OFP8) encode, RNE + satfinite                                   */
 /* ------------------------------------------------------------------------- */
 

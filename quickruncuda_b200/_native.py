@@ -32,6 +32,9 @@ MODE_SIDE_AWARE = 0
 MODE_IGNORE_PAGE_BITS = 1
 MODE_WRONG_SIDE = 2
 MODE_STREAM = 3
+OP_ABSMAX, OP_MAX, OP_MIN, OP_SUM, OP_SUMSQ = 0, 1, 2, 3, 4
+OP_NAMES = {"absmax": OP_ABSMAX, "max": OP_MAX, "min": OP_MIN, "sum": OP_SUM, "sumsq": OP_SUMSQ}
+
 SCHED_AUTO = 0x00
 SCHED_STATIC = 0x10
 SCHED_QUEUE = 0x20
@@ -65,6 +68,7 @@ SIGNATURES = [
     ("qrc_ctx_set_pipeline", c_int, [c_void_p, c_int]),
     ("qrc_ctx_set_overlap", c_int, [c_void_p, c_int]),
     ("qrc_absmax_f32", c_int, [c_void_p, c_size, c_void_p, c_void_p, c_void_p]),
+    ("qrc_reduce_f32", c_int, [c_void_p, c_size, c_int, c_void_p, c_void_p, c_void_p]),
     ("qrc_absmax_f32_noalloc", c_int, [c_void_p, c_size, c_void_p, c_void_p]),
     ("qrc_absmax_f32_host", c_int, [c_void_p, c_size, ctypes.POINTER(c_float), c_void_p, c_void_p]),
     ("qrc_amax_quant_e4m3", c_int, [c_void_p, c_size, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),

@@ -161,6 +161,22 @@ class SideAwareContext:
                                           _stream_handle(stream, self.device) or None))
         return out
 
+    def reduce(self, x, op: str = "absmax", out=None, n: Optional[int] = None, stream=None):
+        """Side-aware reduction of a float32 CUDA tensor with operator `op`
+        ('absmax', 'max', 'min': 1-element float32 result; 'sum', 'sumsq':
+        1-element float64 result).  Asynchronous."""
+        code = nat.OP_NAMES[op]
+        if n is None:
+            n = int(x.numel())
+        if out is None:
+            import torch
+            dt = torch.float64 if code in (nat.OP_SUM, nat.OP_SUMSQ) else torch.float32
+            out = torch.empty(1, dtype=dt, device=f"cuda:{self.device}")
+        nat.check(self.lib, "qrc_reduce_f32",
+                  self.lib.qrc_reduce_f32(_ptr(x) or None, n, code, _ptr(out), self.handle,
+                                          _stream_handle(stream, self.device) or None))
+        return out
+
     def absmax_host(self, x, n: Optional[int] = None, stream=None) -> float:
         """Same from a host buffer (numpy array or CPU tensor); synchronous."""
         if n is None:

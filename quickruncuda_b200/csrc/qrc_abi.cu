@@ -33,6 +33,13 @@ qrc_k_absmax_f32(const float* in, qrc_u64 n, qrc_u32* map, float* out, qrc_u32 m
     qrc::reduce_run<qrc::OpAbsF32>(in, n, map, out, nullptr, mode);
 }
 
+// The other operators of qrc_reduce_f32 (absmax keeps its own kernel name).
+template <class Op, int T>
+__global__ void __launch_bounds__(T, 1024 / T)
+qrc_k_reduce_f32(const float* in, qrc_u64 n, qrc_u32* map, void* out, qrc_u32 mode) {
+    qrc::reduce_run<Op>(in, n, map, out, nullptr, mode);
+}
+
 template <int T>
 __global__ void __launch_bounds__(T, 1024 / T)
 qrc_k_amax_bf16(const uint16_t* in, qrc_u64 n, qrc_u32* map, float* amax, float* scale, qrc_u32 mode) {
@@ -350,6 +357,47 @@ QRC_API int qrc_absmax_f32(const float* d_in, size_t n, float* d_out, qrc_ctx* c
     DeviceScope scope(c->device);
     if (!scope.ok) return QRC_ERR_STATE;
     return launch_absmax(c, d_in, n, d_out, as_stream(stream));
+}
+
+template <class Op, int T>
+static cudaError_t launch_reduce_t(qrc_ctx* c, const float* in, qrc_u64 n, void* out, size_t smem, cudaStream_t s) {
+    static size_t granted = 0;                      // per process, as allow_smem
+    if (smem > granted) {
+        cudaError_t e = cudaFuncSetAttribute(qrc_k_reduce_f32<Op, T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)smem);
+        if (e != cudaSuccess) return e;
+        granted = smem;
+    }
+    return launch(c, qrc_k_reduce_f32<Op, T>, c->num_sms * c->blocks_per_sm, T, smem, s, in, n, c->d_map, out,
+                  (qrc_u32)c->mode);
+}
+
+template <class Op>
+static int launch_reduce(qrc_ctx* c, const float* in, size_t n, void* out, cudaStream_t s) {
+    const size_t smem = launch_smem(c);
+    switch (c->threads) {
+        case 1024: QRC_CK((launch_reduce_t<Op, 1024>(c, in, n, out, smem, s))); break;
+        case 512:  QRC_CK((launch_reduce_t<Op, 512>(c, in, n, out, smem, s))); break;
+        default:   QRC_CK((launch_reduce_t<Op, 256>(c, in, n, out, smem, s))); break;
+    }
+    return QRC_OK;
+}
+
+QRC_API int qrc_reduce_f32(const float* d_in, size_t n, int op, void* d_out, qrc_ctx* c, void* stream) {
+    if (!c || !d_out || (n && !d_in) || ((uintptr_t)d_in & 3)) return QRC_ERR_INVALID;
+    if (op < QRC_OP_ABSMAX || op > QRC_OP_SUMSQ) return QRC_ERR_INVALID;
+    if (op >= QRC_OP_SUM && ((uintptr_t)d_out & 7)) return QRC_ERR_INVALID;
+    if (n > ((size_t)1 << 61)) return QRC_ERR_RANGE;
+    DeviceScope scope(c->device);
+    if (!scope.ok) return QRC_ERR_STATE;
+    cudaStream_t s = as_stream(stream);
+    switch (op) {
+        case QRC_OP_ABSMAX: return launch_absmax(c, d_in, n, (float*)d_out, s);
+        case QRC_OP_MAX: return launch_reduce<qrc::OpMaxF32>(c, d_in, n, d_out, s);
+        case QRC_OP_MIN: return launch_reduce<qrc::OpMinF32>(c, d_in, n, d_out, s);
+        case QRC_OP_SUM: return launch_reduce<qrc::OpSumF32>(c, d_in, n, d_out, s);
+        default: return launch_reduce<qrc::OpSumSqF32>(c, d_in, n, d_out, s);
+    }
 }
 
 QRC_API int qrc_absmax_f32_host(const float* h_in, size_t n, float* h_out, qrc_ctx* c, void* stream) {

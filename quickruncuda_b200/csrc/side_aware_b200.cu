@@ -176,6 +176,7 @@ enum : qrc_u32 {
     H_QUEUE0 = 32, H_QUEUE1 = 64,                  // each on its own 128-byte line
     H_ERR = 96, H_ERR_ADDR_LO = 97, H_ERR_ADDR_HI = 98, H_WAIT_ERR = 99,
     H_COV_BYTES_LO = 100, H_COV_BYTES_HI = 101, H_COV_XOR_LO = 102, H_COV_XOR_HI = 103,
+    H_ACC64 = 104,                                 // 8-byte aligned double accumulator (sums), 104..105
     O_BITLAT = 128,                                // 21 raw latencies of the mask probes
     O_SM_SIDE = 256,                               // per SM: 0 unknown, else 1 + side + 2 * index within side
     O_SM_LAT = 512,                                // per SM raw anchor latency (cycles)
@@ -486,6 +487,28 @@ QRC_DEV float absmax_step(float acc, float x) {
     return r;
 }
 
+// acc = maxNum(acc, x) and minNum(acc, x).
+QRC_DEV float max_step(float acc, float x) {
+    float r;
+    asm("max.f32 %0, %1, %2;" : "=f"(r) : "f"(acc), "f"(x));
+    return r;
+}
+QRC_DEV float min_step(float acc, float x) {
+    float r;
+    asm("min.f32 %0, %1, %2;" : "=f"(r) : "f"(acc), "f"(x));
+    return r;
+}
+
+// Order-preserving map of float bits to unsigned keys: key(a) < key(b) when
+// a < b, and -0 below +0.
+QRC_DEV qrc_u32 float_key(float f) {
+    const qrc_u32 b = __float_as_uint(f);
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+QRC_DEV float key_float(qrc_u32 k) {
+    return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
+}
+
 // Same on two packed bf16 lanes (max.bf16x2 is maxNum as well).
 QRC_DEV qrc_u32 absmax_step_bf16x2(qrc_u32 acc, qrc_u32 x) {
     qrc_u32 r;
@@ -524,12 +547,24 @@ QRC_DEV void ld_stream32(qrc_u64 addr, uint4& a, uint4& b) {
 }
 #endif
 
-// Element operators.  Acc starts at +0; to_bits() returns the accumulator as
-// the bit pattern of a non-negative float, so block/grid maxima can use
-// unsigned integer max.
+// Element operators.  Each gives its accumulator (Acc) and how a thread steps
+// it over 16 loaded bytes or one element; to_red() turns a thread's
+// accumulator into the value the block and the grid combine, through its
+// Finish: FinishMaxU32 (unsigned max on 32-bit keys, neutral 0) or
+// FinishSumF64 (double addition).  Idempotent operators may read an element
+// twice; the others need every element exactly once.  publish() writes the
+// launch's result (NaN when a bounded wait gave up).
+struct FinishMaxU32;
+struct FinishSumF64;
+QRC_DEV float e4m3_scale_from_amax(float amax);
+QRC_DEV float qrc_nan() { return __uint_as_float(0x7FFFFFFFu); }
+
+// max |x| (maxNum: NaN elements lose; empty gives +0).  Result float.
 struct OpAbsF32 {
     typedef float Acc;
+    typedef FinishMaxU32 Finish;
     static constexpr int kElem = 4;
+    static constexpr bool kIdempotent = true;
     QRC_DEV Acc zero() { return 0.0f; }
     QRC_DEV Acc step16(Acc a, uint4 v) {
         a = absmax_step(a, __uint_as_float(v.x)); a = absmax_step(a, __uint_as_float(v.y));
@@ -537,12 +572,20 @@ struct OpAbsF32 {
         return a;
     }
     QRC_DEV Acc step_elem(Acc a, qrc_u64 addr) { return absmax_step(a, *(const float*)addr); }
-    QRC_DEV qrc_u32 to_bits(Acc a) { return __float_as_uint(a); }
+    QRC_DEV Acc merge(Acc a, Acc b) { return max_step(a, b); }
+    QRC_DEV qrc_u32 to_red(Acc a) { return __float_as_uint(a); }   // a >= +0: bits order like values
+    QRC_DEV void publish(void* out, float*, qrc_u32 r, bool err) {
+        *(float*)out = err ? qrc_nan() : __uint_as_float(r);
+    }
 };
 
+// max |x| of bf16 elements, two lanes per accumulator; publishes amax as a
+// float and, when asked, the e4m3 scale 448 / amax.
 struct OpAbsBF16 {
     typedef qrc_u32 Acc;   // two bf16 lanes
+    typedef FinishMaxU32 Finish;
     static constexpr int kElem = 2;
+    static constexpr bool kIdempotent = true;
     QRC_DEV Acc zero() { return 0u; }
     QRC_DEV Acc step16(Acc a, uint4 v) {
         a = absmax_step_bf16x2(a, v.x); a = absmax_step_bf16x2(a, v.y);
@@ -552,9 +595,107 @@ struct OpAbsBF16 {
     QRC_DEV Acc step_elem(Acc a, qrc_u64 addr) {
         return absmax_step_bf16x2(a, (qrc_u32)(*(const unsigned short*)addr));
     }
-    QRC_DEV qrc_u32 to_bits(Acc a) {
+    QRC_DEV Acc merge(Acc a, Acc b) { return absmax_step_bf16x2(a, b); }
+    QRC_DEV qrc_u32 to_red(Acc a) {
         const qrc_u32 lo = a << 16, hi = a & 0xFFFF0000u;   // bf16 -> f32 bits, both >= +0
         return lo > hi ? lo : hi;
+    }
+    QRC_DEV void publish(void* out, float* scale_out, qrc_u32 r, bool err) {
+        const float amax = err ? qrc_nan() : __uint_as_float(r);
+        *(float*)out = amax;
+        if (scale_out) *scale_out = e4m3_scale_from_amax(amax);
+    }
+};
+
+// max x (maxNum: NaN elements lose; empty or all-NaN gives -inf).
+struct OpMaxF32 {
+    typedef float Acc;
+    typedef FinishMaxU32 Finish;
+    static constexpr int kElem = 4;
+    static constexpr bool kIdempotent = true;
+    QRC_DEV Acc zero() { return __uint_as_float(0xFF800000u); }
+    QRC_DEV Acc step16(Acc a, uint4 v) {
+        a = max_step(a, __uint_as_float(v.x)); a = max_step(a, __uint_as_float(v.y));
+        a = max_step(a, __uint_as_float(v.z)); a = max_step(a, __uint_as_float(v.w));
+        return a;
+    }
+    QRC_DEV Acc step_elem(Acc a, qrc_u64 addr) { return max_step(a, *(const float*)addr); }
+    QRC_DEV Acc merge(Acc a, Acc b) { return max_step(a, b); }
+    QRC_DEV qrc_u32 to_red(Acc a) { return float_key(a); }      // key(-inf) > 0, the neutral
+    QRC_DEV void publish(void* out, float*, qrc_u32 r, bool err) {
+        *(float*)out = err ? qrc_nan() : (r < float_key(zero()) ? zero() : key_float(r));
+    }
+};
+
+// min x (minNum: NaN elements lose; empty or all-NaN gives +inf).  The grid
+// combines complemented keys with unsigned max.
+struct OpMinF32 {
+    typedef float Acc;
+    typedef FinishMaxU32 Finish;
+    static constexpr int kElem = 4;
+    static constexpr bool kIdempotent = true;
+    QRC_DEV Acc zero() { return __uint_as_float(0x7F800000u); }
+    QRC_DEV Acc step16(Acc a, uint4 v) {
+        a = min_step(a, __uint_as_float(v.x)); a = min_step(a, __uint_as_float(v.y));
+        a = min_step(a, __uint_as_float(v.z)); a = min_step(a, __uint_as_float(v.w));
+        return a;
+    }
+    QRC_DEV Acc step_elem(Acc a, qrc_u64 addr) { return min_step(a, *(const float*)addr); }
+    QRC_DEV Acc merge(Acc a, Acc b) { return min_step(a, b); }
+    QRC_DEV qrc_u32 to_red(Acc a) { return ~float_key(a); }
+    QRC_DEV void publish(void* out, float*, qrc_u32 r, bool err) {
+        *(float*)out = err ? qrc_nan() : (r < ~float_key(zero()) ? zero() : key_float(~r));
+    }
+};
+
+// sum of x, accumulated in double (every element exactly once; NaN and
+// infinities propagate as in IEEE addition).  Result double.
+struct OpSumF32 {
+    typedef double Acc;
+    typedef FinishSumF64 Finish;
+    static constexpr int kElem = 4;
+    static constexpr bool kIdempotent = false;
+    QRC_DEV Acc zero() { return 0.0; }
+    // Widening and adding in one asm block keeps the compiler from widening
+    // all 32 loaded floats of a batch at once (which spilled).
+    QRC_DEV Acc add(Acc a, qrc_u32 x) {
+        double r;
+        asm("{\n\t.reg .f64 t;\n\tcvt.f64.f32 t, %2;\n\tadd.rn.f64 %0, %1, t;\n\t}" : "=d"(r) : "d"(a), "r"(x));
+        return r;
+    }
+    QRC_DEV Acc step16(Acc a, uint4 v) {
+        a = add(a, v.x); a = add(a, v.y); a = add(a, v.z); a = add(a, v.w);
+        return a;
+    }
+    QRC_DEV Acc step_elem(Acc a, qrc_u64 addr) { return add(a, *(const qrc_u32*)addr); }
+    QRC_DEV Acc merge(Acc a, Acc b) { return a + b; }
+    QRC_DEV double to_red(Acc a) { return a; }
+    QRC_DEV void publish(void* out, float*, double r, bool err) {
+        *(double*)out = err ? __longlong_as_double(0x7FF8000000000000ll) : r;
+    }
+};
+
+// sum of x*x in double (fma per element).  Result double.
+struct OpSumSqF32 {
+    typedef double Acc;
+    typedef FinishSumF64 Finish;
+    static constexpr int kElem = 4;
+    static constexpr bool kIdempotent = false;
+    QRC_DEV Acc zero() { return 0.0; }
+    QRC_DEV Acc sq(Acc a, qrc_u32 x) {         // a + x*x, the square exact in double
+        double r;
+        asm("{\n\t.reg .f64 t;\n\tcvt.f64.f32 t, %2;\n\tfma.rn.f64 %0, t, t, %1;\n\t}" : "=d"(r) : "d"(a), "r"(x));
+        return r;
+    }
+    QRC_DEV Acc step16(Acc a, uint4 v) {
+        a = sq(a, v.x); a = sq(a, v.y); a = sq(a, v.z); a = sq(a, v.w);
+        return a;
+    }
+    QRC_DEV Acc step_elem(Acc a, qrc_u64 addr) { return sq(a, *(const qrc_u32*)addr); }
+    QRC_DEV Acc merge(Acc a, Acc b) { return a + b; }
+    QRC_DEV double to_red(Acc a) { return a; }
+    QRC_DEV void publish(void* out, float*, double r, bool err) {
+        *(double*)out = err ? __longlong_as_double(0x7FF8000000000000ll) : r;
     }
 };
 
@@ -984,6 +1125,49 @@ QRC_DEV qrc_u32 block_max(qrc_u32 bits) {
     return s_res;
 }
 
+// Sum of `v` over the block, returned to every thread.
+QRC_DEV double block_sum_f64(double v) {
+    __shared__ double s_wd[32];
+    __shared__ double s_resd;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, W = blockDim.x >> 5;
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+    if (lane == 0) s_wd[warp] = v;
+    __syncthreads();
+    if (warp == 0) {
+        double x = lane < W ? s_wd[lane] : 0.0;
+        for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xFFFFFFFFu, x, o);
+        if (lane == 0) s_resd = x;
+    }
+    __syncthreads();
+    return s_resd;
+}
+
+// How blocks and the grid combine an operator's values (see the element
+// operators): block(), a fire-and-forget global reduction into the map, and
+// the last CTA's take-and-reset of the global accumulator.
+struct FinishMaxU32 {
+    typedef qrc_u32 Red;
+    QRC_DEV Red neutral() { return 0u; }
+    QRC_DEV Red block(Red v) { return block_max(v); }
+    QRC_DEV Red combine(Red a, Red b) { return a > b ? a : b; }
+    QRC_DEV void red(qrc_u32* map, Red v) {
+        asm volatile("red.relaxed.gpu.global.max.u32 [%0], %1;" :: "l"(&map[H_ACC]), "r"(v) : "memory");
+    }
+    QRC_DEV Red take(qrc_u32* map) { return atomicExch(&map[H_ACC], 0u); }
+};
+struct FinishSumF64 {
+    typedef double Red;
+    QRC_DEV Red neutral() { return 0.0; }
+    QRC_DEV Red block(Red v) { return block_sum_f64(v); }
+    QRC_DEV Red combine(Red a, Red b) { return a + b; }
+    QRC_DEV void red(qrc_u32* map, Red v) {
+        asm volatile("red.relaxed.gpu.global.add.f64 [%0], %1;" :: "l"(&map[H_ACC64]), "d"(v) : "memory");
+    }
+    QRC_DEV Red take(qrc_u32* map) {
+        return __longlong_as_double((long long)atomicExch((unsigned long long*)&map[H_ACC64], 0ull));
+    }
+};
+
 // Static shares (see reduce_run).  All K_s SMs of side s take part; the two
 // sides are not paired, each covers its own chunk of every pair.
 // A 256-thread group reads the side-s chunks of 8 consecutive pairs at once:
@@ -1163,7 +1347,8 @@ QRC_DEV typename Op::Acc read_tail(typename Op::Acc acc, const ChunkMap& w, qrc_
 // Bulk pipeline (dynamic shared memory for >= 2 slots per warp): queues only.
 // Mode 3: side-agnostic grid-stride stream.
 template <class Op>
-QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, float* out, float* scale_out, qrc_u32 mode) {
+QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, void* out, float* scale_out, qrc_u32 mode) {
+    typedef typename Op::Finish Fin;
     const qrc_u32 sched = mode & SCHED_MASK;
     mode &= ~SCHED_MASK;
     const qrc_u64 a = (qrc_u64)A, bytes = n * (qrc_u64)Op::kElem, end = a + bytes;
@@ -1235,9 +1420,24 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, float* out, floa
             qrc_u32 first = 0;
             if (tail && (threadIdx.x & 255) == 0) first = atomicAdd(&map[cm.side ? H_QUEUE1 : H_QUEUE0], 1u);
             if (own_share) {
-                if (threadIdx.x == 0) *(volatile qrc_u32*)&map[O_CLAIMS + 128 * cm.side + own_k] = 1u;
-                acc = plain ? read_share<Op, 0>(acc, cm, sh, cm.side, own_k, pw0 QRC_CS_ARG)
-                            : read_share<Op>(acc, cm, sh, cm.side, own_k, pw0 QRC_CS_ARG);
+                if constexpr (Op::kIdempotent) {
+                    // two CTAs on one SM both read the share: harmless
+                    if (threadIdx.x == 0) *(volatile qrc_u32*)&map[O_CLAIMS + 128 * cm.side + own_k] = 1u;
+                    acc = plain ? read_share<Op, 0>(acc, cm, sh, cm.side, own_k, pw0 QRC_CS_ARG)
+                                : read_share<Op>(acc, cm, sh, cm.side, own_k, pw0 QRC_CS_ARG);
+                } else {
+                    // Exactly once: the first CTA to set the mark owns the
+                    // share.  The share is read into its own accumulator
+                    // while the claim is in flight, and dropped if it lost.
+                    __shared__ qrc_u32 s_lost;
+                    qrc_u32 old = 0;
+                    if (threadIdx.x == 0) old = atomicExch(&map[O_CLAIMS + 128 * cm.side + own_k], 1u);
+                    typename Op::Acc part = plain ? read_share<Op, 0>(Op::zero(), cm, sh, cm.side, own_k, pw0 QRC_CS_ARG)
+                                                  : read_share<Op>(Op::zero(), cm, sh, cm.side, own_k, pw0 QRC_CS_ARG);
+                    if (threadIdx.x == 0) s_lost = old;
+                    __syncthreads();
+                    if (!s_lost) acc = Op::merge(acc, part);
+                }
             }
             if (tail) acc = read_tail<Op>(acc, cm, sh.R, map, cm.side, first QRC_CS_ARG);
         } else {
@@ -1299,21 +1499,21 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, float* out, floa
     cov_flush(cs, lane, map);
 #endif
 
-    // ---- finish: block maximum, one reduction, ticket --------------------
-    const qrc_u32 v = block_max(Op::to_bits(acc));
+    // ---- finish: block value, one global reduction, ticket ----------------
+    const typename Fin::Red v = Fin::block(Op::to_red(acc));
     __shared__ int s_last;
     if (threadIdx.x == 0) {
         qrc_u32 t;
 #if QRC_FINISH == 1
-        // The block's maximum goes out as a fire-and-forget reduction; the
+        // The block's value goes out as a fire-and-forget reduction; the
         // ticket increment has release semantics (ordered after it) and
         // acquire semantics (the last CTA then sees every other CTA's
         // reduction and share mark).
-        asm volatile("red.relaxed.gpu.global.max.u32 [%0], %1;" :: "l"(&map[H_ACC]), "r"(v) : "memory");
+        Fin::red(map, v);
         asm volatile("atom.acq_rel.gpu.global.inc.u32 %0, [%1], %2;"
                      : "=r"(t) : "l"(&map[H_RUN_TICKET]), "r"(gridDim.x - 1) : "memory");
 #else
-        atomicMax(&map[H_ACC], v);
+        Fin::red(map, v);
         __threadfence();
         t = atomicInc(&map[H_RUN_TICKET], gridDim.x - 1);
         __threadfence();
@@ -1326,10 +1526,11 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, float* out, floa
     // ---- last CTA: unmarked shares, then publish ---------------------------
     // Thread 0 takes the accumulator while warp 0 checks the share marks, in
     // the same round trip; only a missing share costs more.
-    __shared__ qrc_u32 s_acc, s_wait_err;
+    __shared__ typename Fin::Red s_acc;
+    __shared__ qrc_u32 s_wait_err;
     __shared__ int s_share;
     if (threadIdx.x == 0) {
-        s_acc = atomicExch(&map[H_ACC], 0u);
+        s_acc = Fin::take(map);
         s_wait_err = __ldcg(&map[H_WAIT_ERR]);
     }
     typename Op::Acc acc2 = Op::zero();
@@ -1369,20 +1570,18 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, float* out, floa
     } else {
         __syncthreads();
     }
-    const qrc_u32 v2 = extra ? block_max(Op::to_bits(acc2)) : 0u;
+    const typename Fin::Red v2 = extra ? Fin::block(Op::to_red(acc2)) : Fin::neutral();
     if (threadIdx.x == 0) {
-        qrc_u32 r = s_acc;
-        r = r > v2 ? r : v2;
+        const typename Fin::Red r = Fin::combine(s_acc, v2);
         map[H_QUEUE0] = 0u;
         map[H_QUEUE1] = 0u;
-        if (s_wait_err) r = 0x7FFFFFFFu;        // a bounded wait gave up: no valid maximum
-        out[0] = __uint_as_float(r);
+        // a bounded wait that gave up leaves no valid result: NaN
+        Op::publish(out, scale_out, r, s_wait_err != 0u);
 #if QRC_TIMELINE
         qrc_u64 t_fin;
         asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_fin));
         map[O_TIMELINE + 1023] = (qrc_u32)t_fin;      // end of the launch's last CTA
 #endif
-        if (scale_out) scale_out[0] = e4m3_scale_from_amax(__uint_as_float(r));
     }
 }
 
@@ -1398,6 +1597,30 @@ init(float* A, unsigned int* side_map, float* C, int num_dwords, int arg1, int a
     qrc::discover(A, num_dwords > 0 ? (qrc_u64)num_dwords * 4ull : 0ull, side_map);
 }
 
+// The operator is chosen when the file is compiled, as in the reference,
+// whose reduction_op is edited in place (side_aware.cu:215-219):
+// -H '#define QRC_PLUGIN_OP n' with n = 0 absmax (default), 1 max, 2 min,
+// 3 sum, 4 sum of squares.  C[0] receives the result as a float (sums are
+// accumulated in double and rounded once at the end).
+#ifndef QRC_PLUGIN_OP
+#define QRC_PLUGIN_OP 0
+#endif
+namespace qrc {
+template <class Op>
+struct FloatOut : Op {                 // a double result rounded to one float in C[0]
+    QRC_DEV void publish(void* out, float* s, double r, bool err) {
+        double d;
+        Op::publish(&d, s, r, err);
+        *(float*)out = (float)d;
+    }
+};
+template <int K> struct PluginOp { typedef OpAbsF32 T; };
+template <> struct PluginOp<1> { typedef OpMaxF32 T; };
+template <> struct PluginOp<2> { typedef OpMinF32 T; };
+template <> struct PluginOp<3> { typedef FloatOut<OpSumF32> T; };
+template <> struct PluginOp<4> { typedef FloatOut<OpSumSqF32> T; };
+}  // namespace qrc
+
 extern "C" __global__ void __launch_bounds__(1024, 1)
 kernel(float* A, unsigned int* side_map, float* C, int num_dwords, int mode, int arg2) {
     (void)arg2;
@@ -1406,8 +1629,8 @@ kernel(float* A, unsigned int* side_map, float* C, int num_dwords, int mode, int
 #elif defined(FORCE_RANDOM_SIDE)
     mode = (mode & qrc::SCHED_MASK) | qrc::MODE_IGNORE_PAGE_BITS;
 #endif
-    qrc::reduce_run<qrc::OpAbsF32>(A, num_dwords > 0 ? (qrc_u64)num_dwords : 0ull, side_map, C, nullptr,
-                                   (qrc_u32)mode);
+    qrc::reduce_run<qrc::PluginOp<QRC_PLUGIN_OP>::T>(A, num_dwords > 0 ? (qrc_u64)num_dwords : 0ull, side_map, C,
+                                                     nullptr, (qrc_u32)mode);
 }
 #endif  // QRC_NO_PLUGIN_ABI
 

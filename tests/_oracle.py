@@ -42,6 +42,10 @@ class Oracle:
             ("oracle_absmax_f32_serial", f32, [_f32p, sz]),
             ("oracle_absmax_f32", f32, [_f32p, sz, i32, ctypes.POINTER(i32)]),
             ("oracle_absmax_bf16", f32, [_u16p, sz]),
+            ("oracle_max_f32", f32, [_f32p, sz]),
+            ("oracle_min_f32", f32, [_f32p, sz]),
+            ("oracle_sum_f32", ctypes.c_double, [_f32p, sz, ctypes.POINTER(ctypes.c_double)]),
+            ("oracle_sumsq_f32", ctypes.c_double, [_f32p, sz, ctypes.POINTER(ctypes.c_double)]),
             ("oracle_f32_to_e4m3", ctypes.c_uint8, [f32]),
             ("oracle_e4m3_to_f32", f32, [ctypes.c_uint8]),
             ("oracle_f32_bits_to_e4m3", None, [u32, sz, _u8p]),
@@ -105,6 +109,18 @@ class Oracle:
     def absmax_serial(self, x: np.ndarray) -> np.float32:
         x = np.ascontiguousarray(x, dtype=np.float32)
         return np.float32(self.lib.oracle_absmax_f32_serial(_p(x, _f32p), x.size))
+
+    def reduce(self, op: str, x: np.ndarray):
+        """op in absmax/max/min (np.float32 result) or sum/sumsq (returns
+        (float result, sum of |term|) for the error bound)."""
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        if op == "absmax":
+            return self.absmax(x)
+        if op in ("max", "min"):
+            return np.float32(getattr(self.lib, f"oracle_{op}_f32")(_p(x, _f32p), x.size))
+        a = ctypes.c_double()
+        r = getattr(self.lib, f"oracle_{op}_f32")(_p(x, _f32p), x.size, ctypes.byref(a))
+        return float(r), float(a.value)
 
     def absmax_bf16(self, x: np.ndarray) -> np.float32:
         x = np.ascontiguousarray(x, dtype=np.uint16)

@@ -59,6 +59,7 @@ def test_invalid_arguments_rejected_without_gpu(lib):
     assert lib.qrc_absmax_f32(None, 16, None, None, None) == -1
     assert lib.qrc_ctx_create(None, 0, None, 0, None) == -1
     assert lib.qrc_ctx_set_mode(None, 0) == -1
+    assert lib.qrc_reduce_f32(None, 16, 3, None, None, None) == -1
     assert lib.qrc_ctx_destroy(None) == 0
 
 
@@ -83,7 +84,8 @@ def _harness(*args, check=True):
 
 
 @pytest.mark.parametrize("arch", ["sm_100a", "sm_100"])
-@pytest.mark.parametrize("header", ["", "#define FORCE_RANDOM_SIDE", "#define FORCE_WRONG_SIDE"])
+@pytest.mark.parametrize("header", ["", "#define FORCE_RANDOM_SIDE", "#define FORCE_WRONG_SIDE",
+                                    "#define QRC_PLUGIN_OP 2", "#define QRC_PLUGIN_OP 4"])
 def test_kernel_file_compiles_with_nvrtc(arch, header):
     # The reference harness compiles kernel files with NVRTC, fast math and
     # C++17 for sm_100 on B200 (utils/cuda_helper.h:223-253); ours defaults to sm_100a.

@@ -224,3 +224,31 @@ def test_oracle_matches_reference_outputs(oracle, case):
     if case.get("reference_defect"):
         pytest.skip(f"reference output affected by a documented defect: {case['reference_defect']}")
     assert got == case["c0_bits"], (hex(got), hex(case["c0_bits"]))
+
+
+def test_other_operators_semantics(oracle):
+    """max/min skip NaN and order -0 below +0; empty gives -inf/+inf; sums are
+    compensated (exact here) and report sum |term| for error bounds."""
+    nan, inf = np.float32("nan"), np.float32("inf")
+    x = np.array([1.5, -3.0, nan, 2.5, -0.0, 0.0], np.float32)
+    assert oracle.reduce("max", x) == np.float32(2.5)
+    assert oracle.reduce("min", x) == np.float32(-3.0)
+    z = np.array([0.0, -0.0], np.float32)
+    assert np.signbit(oracle.reduce("min", z)) and not np.signbit(oracle.reduce("max", z))
+    assert oracle.reduce("max", np.array([], np.float32)) == -inf
+    assert oracle.reduce("min", np.array([nan], np.float32)) == inf
+    s, a = oracle.reduce("sum", np.array([1e8, 1.0, -1e8, 0.5], np.float32))
+    assert s == 1.5 and a == 2e8 + 1.5
+    s, a = oracle.reduce("sumsq", np.array([3.0, -4.0], np.float32))
+    assert s == 25.0 and a == 25.0
+    assert np.isnan(oracle.reduce("sum", x)[0])
+    assert oracle.reduce("sum", np.array([inf, 1.0], np.float32))[0] == np.inf
+
+
+def test_sum_matches_exact_fraction_sum(oracle):
+    from fractions import Fraction
+    rng = np.random.default_rng(5)
+    x = (rng.standard_normal(2000) * 10.0 ** rng.integers(-8, 9, 2000)).astype(np.float32)
+    exact = sum(Fraction(float(v)) for v in x)
+    s, a = oracle.reduce("sum", x)
+    assert abs(Fraction(s) - exact) <= Fraction(2.0 ** -52) * abs(exact) + Fraction(2.0 ** -100)
