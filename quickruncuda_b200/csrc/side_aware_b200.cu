@@ -516,6 +516,11 @@ QRC_DEV qrc_u32 absmax_step_bf16x2(qrc_u32 acc, qrc_u32 x) {
     return r;
 }
 
+// Sixteen bytes of an operator's neutral element: fills the load slots of a
+// partial batch, which are stepped like the others.
+template <class Op>
+QRC_DEV uint4 pad16() { return make_uint4(Op::kPad, Op::kPad, Op::kPad, Op::kPad); }
+
 // Streaming 16-byte load (flavour chosen by QRC_LOAD_KIND).
 template <int Kind>
 QRC_DEV uint4 ld16(qrc_u64 addr) {
@@ -565,6 +570,7 @@ struct OpAbsF32 {
     typedef FinishMaxU32 Finish;
     static constexpr int kElem = 4;
     static constexpr bool kIdempotent = true;
+    static constexpr qrc_u32 kPad = 0u;   // element bits that leave the accumulator unchanged
     QRC_DEV Acc zero() { return 0.0f; }
     QRC_DEV Acc step16(Acc a, uint4 v) {
         a = absmax_step(a, __uint_as_float(v.x)); a = absmax_step(a, __uint_as_float(v.y));
@@ -586,6 +592,7 @@ struct OpAbsBF16 {
     typedef FinishMaxU32 Finish;
     static constexpr int kElem = 2;
     static constexpr bool kIdempotent = true;
+    static constexpr qrc_u32 kPad = 0u;   // element bits that leave the accumulator unchanged
     QRC_DEV Acc zero() { return 0u; }
     QRC_DEV Acc step16(Acc a, uint4 v) {
         a = absmax_step_bf16x2(a, v.x); a = absmax_step_bf16x2(a, v.y);
@@ -613,6 +620,7 @@ struct OpMaxF32 {
     typedef FinishMaxU32 Finish;
     static constexpr int kElem = 4;
     static constexpr bool kIdempotent = true;
+    static constexpr qrc_u32 kPad = 0xFF800000u;   // element bits that leave the accumulator unchanged
     QRC_DEV Acc zero() { return __uint_as_float(0xFF800000u); }
     QRC_DEV Acc step16(Acc a, uint4 v) {
         a = max_step(a, __uint_as_float(v.x)); a = max_step(a, __uint_as_float(v.y));
@@ -634,6 +642,7 @@ struct OpMinF32 {
     typedef FinishMaxU32 Finish;
     static constexpr int kElem = 4;
     static constexpr bool kIdempotent = true;
+    static constexpr qrc_u32 kPad = 0x7F800000u;   // element bits that leave the accumulator unchanged
     QRC_DEV Acc zero() { return __uint_as_float(0x7F800000u); }
     QRC_DEV Acc step16(Acc a, uint4 v) {
         a = min_step(a, __uint_as_float(v.x)); a = min_step(a, __uint_as_float(v.y));
@@ -655,6 +664,7 @@ struct OpSumF32 {
     typedef FinishSumF64 Finish;
     static constexpr int kElem = 4;
     static constexpr bool kIdempotent = false;
+    static constexpr qrc_u32 kPad = 0u;   // element bits that leave the accumulator unchanged
     QRC_DEV Acc zero() { return 0.0; }
     // Widening and adding in one asm block keeps the compiler from widening
     // all 32 loaded floats of a batch at once (which spilled).
@@ -681,6 +691,7 @@ struct OpSumSqF32 {
     typedef FinishSumF64 Finish;
     static constexpr int kElem = 4;
     static constexpr bool kIdempotent = false;
+    static constexpr qrc_u32 kPad = 0u;   // element bits that leave the accumulator unchanged
     QRC_DEV Acc zero() { return 0.0; }
     QRC_DEV Acc sq(Acc a, qrc_u32 x) {         // a + x*x, the square exact in double
         double r;
@@ -751,7 +762,7 @@ QRC_DEV typename Op::Acc chunk_warp(typename Op::Acc acc, qrc_u64 chunk, int n51
             uint4 v[8];
             #pragma unroll
             for (int u = 0; u < 4; u++) {
-                v[2 * u] = v[2 * u + 1] = make_uint4(0u, 0u, 0u, 0u);
+                v[2 * u] = v[2 * u + 1] = pad16<Op>();
                 if (k + u < n1k) ld_stream32(base + 1024ull * (k + u), v[2 * u], v[2 * u + 1]);
             }
             #pragma unroll
@@ -765,7 +776,7 @@ QRC_DEV typename Op::Acc chunk_warp(typename Op::Acc acc, qrc_u64 chunk, int n51
         uint4 v[8];
         #pragma unroll
         for (int u = 0; u < 8; u++) {
-            v[u] = make_uint4(0u, 0u, 0u, 0u);
+            v[u] = pad16<Op>();
             const qrc_u64 x = base + 512ull * (k + u);
             if (k + u < n512) { QRC_CHECK(x, 16) v[u] = ld16<Kind>(x); }
         }
@@ -782,7 +793,7 @@ QRC_DEV typename Op::Acc chunks_across(typename Op::Acc acc, const qrc_u64* ch, 
         uint4 v[8];
         #pragma unroll
         for (int u = 0; u < 8; u++) {
-            v[u] = make_uint4(0u, 0u, 0u, 0u);
+            v[u] = pad16<Op>();
             const qrc_u64 x = ch[u] + 16ull * lane + 512ull * k;
             if (u < m) { QRC_CHECK(x, 16) v[u] = ld_stream16(x); }
         }
@@ -1232,7 +1243,7 @@ QRC_DEV typename Op::Acc read_share(typename Op::Acc acc, const ChunkMap& w, con
         uint4 v[8];
         #pragma unroll
         for (int j = 0; j < 8; j++) {
-            v[j] = make_uint4(0u, 0u, 0u, 0u);
+            v[j] = pad16<Op>();
             const qrc_u64 pair = b * 8 + j;
             if (pair < npairs) {
                 const qrc_u64 x = w.chunk_of(pair, s) + 16ull * t;
@@ -1301,7 +1312,7 @@ QRC_DEV typename Op::Acc read_tail(typename Op::Acc acc, const ChunkMap& w, qrc_
             } else {
                 #pragma unroll
                 for (int j = 0; j < 8; j++) {
-                    v[j] = make_uint4(0u, 0u, 0u, 0u);
+                    v[j] = pad16<Op>();
                     const qrc_u64 pair = p0 + j;
                     if (pair < w.npairs) {
                         const qrc_u64 x = w.chunk_of(pair, s) + 16ull * t;
@@ -1377,7 +1388,7 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, void* out, float
             uint4 v[8];
             #pragma unroll
             for (int u = 0; u < 8; u++) {
-                v[u] = make_uint4(0u, 0u, 0u, 0u);
+                v[u] = pad16<Op>();
                 const qrc_u64 j = i + u * stride;
                 if (j < nv) { QRC_CHECK(lo + 16 * j, 16) v[u] = ld_stream16(lo + 16 * j); }
             }

@@ -66,6 +66,7 @@ def test_reduce_parity(buf, oracle, op, mode, shape):
 @pytest.mark.parametrize("vals", [
     [0.0, -0.0], [-0.0, 0.0, -0.0], [float("nan"), 1.0, float("-inf")], [float("inf"), -2.0],
     [float("nan")], [-1e-45, 1e-45], [3.0, float("nan"), -7.0, float("inf"), float("-inf")],
+    [2.0, 3.0], [-2.0, -5.0],          # one sign only: partial batches must not add zeros
 ])
 def test_reduce_special_values(cuda, qrc, oracle, vals):
     import torch
