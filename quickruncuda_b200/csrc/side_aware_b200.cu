@@ -1443,11 +1443,20 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, void* out, float
                     __shared__ qrc_u32 s_lost;
                     qrc_u32 old = 0;
                     if (threadIdx.x == 0) old = atomicExch(&map[O_CLAIMS + 128 * cm.side + own_k], 1u);
+#ifdef QRC_CHECKED
+                    // coverage counts only the reads whose values are kept
+                    CheckState cs_all = cs;
+                    cs.bytes = 0; cs.xr = 0;
+#endif
                     typename Op::Acc part = plain ? read_share<Op, 0>(Op::zero(), cm, sh, cm.side, own_k, pw0 QRC_CS_ARG)
                                                   : read_share<Op>(Op::zero(), cm, sh, cm.side, own_k, pw0 QRC_CS_ARG);
                     if (threadIdx.x == 0) s_lost = old;
                     __syncthreads();
                     if (!s_lost) acc = Op::merge(acc, part);
+#ifdef QRC_CHECKED
+                    if (s_lost) { cs.bytes = cs_all.bytes; cs.xr = cs_all.xr; }
+                    else { cs.bytes += cs_all.bytes; cs.xr ^= cs_all.xr; }
+#endif
                 }
             }
             if (tail) acc = read_tail<Op>(acc, cm, sh.R, map, cm.side, first QRC_CS_ARG);
