@@ -53,6 +53,8 @@ def parse_args():
     ap.add_argument("--mode", default="side_aware", choices=["side_aware", "ignore_page_bits", "wrong_side", "stream"])
     ap.add_argument("--sched", default="auto", choices=["auto", "static", "queue", "balanced"],
                     help="work schedule: by size, fixed per-SM shares, per-side queues, or shares plus a queued tail")
+    ap.add_argument("--collective", default="fused", choices=["fused", "nccl"],
+                    help="N>1: cross-GPU max inside the kernel over NVLink peer stores, or an NCCL all-reduce")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-ablation", action="store_true")
@@ -252,8 +254,16 @@ def run_ours(args):
     ctx.schedule = args.sched
     ctx.set_overlap(not args.no_overlap)
     out = torch.zeros(1, dtype=torch.float32, device=dev)
+    px = None
+    if world > 1 and args.collective == "fused":
+        from quickruncuda_b200.sharded import PeerMax
+        px = PeerMax.try_create(ctx)            # None on every rank if peers cannot be mapped
+    collective = ("in-kernel NVLink peer max" if px is not None else "nccl_max_allreduce") if world > 1 else None
 
     def step():
+        if px is not None:
+            px.absmax(x, out)
+            return
         ctx.absmax(x, out=out)
         if world > 1:
             dist.all_reduce(out, op=dist.ReduceOp.MAX)
@@ -431,7 +441,8 @@ def run_ours(args):
                                             "balanced (static shares + queued tail)")),
                    "overlap": not args.no_overlap,
                    "launch": f"{info['num_sms_measured'] or ''} SMs x 1 CTA x 1024 threads",
-                   "l2": L2_NOTE, "parallelism": "replicated shards" if world == 1 else f"shard{world}+nccl_max_allreduce"},
+                   "l2": L2_NOTE,
+                   "parallelism": "replicated shards" if world == 1 else f"shard{world}+{collective}"},
         "roofline": roofline,
         "cpu_baseline": cpu,
         "e2e": e2e,
@@ -447,6 +458,8 @@ def run_ours(args):
         line["per_gpu_gbs"] = round(achieved, 2)
     if rank == 0:
         print(json.dumps(line), flush=True)
+    if px is not None:
+        px.close()
     ctx.close()
     if world > 1:
         dist.barrier()

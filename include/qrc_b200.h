@@ -202,6 +202,32 @@ int qrc_absmax_f32_host(const float* h_in, size_t n, float* h_out, qrc_ctx* ctx,
 int qrc_amax_quant_e4m3(const uint16_t* d_in_bf16, size_t n, uint8_t* d_q, float* d_scale,
                         float* d_amax, qrc_ctx* ctx, void* stream);
 
+/* Sharded absmax with the cross-GPU maximum taken inside the kernel: one
+ * process (rank) per GPU, each reducing its own shard.  The last CTA of each
+ * rank stores its partial maximum in a slot of every rank's exchange array
+ * over NVLink, then waits (bounded, about 2 s) until its own array holds this
+ * launch's value from every rank, and writes the maximum over all ranks.
+ * Set-up, once per process:
+ *   qrc_xchg_create(&x, device, rank, world);
+ *   qrc_xchg_get_handle(x, h)          -> send h (QRC_XCHG_HANDLE_BYTES) to every rank;
+ *   qrc_xchg_set_peer(x, peer, h_peer) for every other rank (CUDA IPC, so
+ *                                         each rank is a separate process).
+ * Every rank must then call qrc_absmax_f32_allreduce the same number of times,
+ * in the same order, like a collective.  If a peer's value does not arrive in
+ * time (a rank died, or calls out of step), *d_out is NaN and the map word
+ * H_XCHG_ERR is set; the context stays usable.
+ * Replaces: a per-GPU qrc_absmax_f32 followed by an NCCL max all-reduce of one
+ * float; the reference has no multi-GPU path (QuickRunCUDA.cpp:286 uses
+ * device 0 only). */
+#define QRC_XCHG_MAX_WORLD 64
+#define QRC_XCHG_HANDLE_BYTES 64
+typedef struct qrc_xchg qrc_xchg;
+int qrc_xchg_create(qrc_xchg** out, int device, int rank, int world);
+int qrc_xchg_get_handle(const qrc_xchg* x, void* handle_out);
+int qrc_xchg_set_peer(qrc_xchg* x, int peer, const void* handle);
+int qrc_xchg_destroy(qrc_xchg* x);
+int qrc_absmax_f32_allreduce(const float* d_in, size_t n, float* d_out, qrc_ctx* ctx, qrc_xchg* x, void* stream);
+
 /* Synthetic inputs generated on the device; element i of the stream is a pure
  * function of (seed, offset + i), so shards of one stream can be generated
  * independently.  uniform[-1,1) on a 2^-23 grid; normal(0, sigma) is the

@@ -38,6 +38,18 @@ int qrc_debug_cvt_e4m3(const float* d_in, size_t n, uint8_t* d_out, void* stream
  * from a test on the same scratch). */
 void* qrc_ctx_map_device_ptr(const struct qrc_ctx* ctx);
 
+/* Exchange tests on one GPU: map a peer's slot array to a local device buffer
+ * (no IPC), read this rank's slot array, and the epoch of the last launch.
+ * With them a test can play a peer from the host (write its slot before the
+ * launch) or leave a slot empty and check that the bounded wait gives up. */
+struct qrc_xchg;
+int qrc_xchg_debug_set_peer_ptr(struct qrc_xchg* x, int peer, void* d_slots);
+/* Write (epoch, value) into this rank's slot for `peer`, as that peer would.
+ * Synchronous. */
+int qrc_xchg_debug_post(struct qrc_xchg* x, int peer, uint32_t epoch, uint32_t value_bits);
+void* qrc_xchg_debug_slots(const struct qrc_xchg* x);
+uint32_t qrc_xchg_epoch(const struct qrc_xchg* x);
+
 #ifdef __cplusplus
 }
 #endif

@@ -69,6 +69,15 @@ SIGNATURES = [
     ("qrc_ctx_set_overlap", c_int, [c_void_p, c_int]),
     ("qrc_absmax_f32", c_int, [c_void_p, c_size, c_void_p, c_void_p, c_void_p]),
     ("qrc_reduce_f32", c_int, [c_void_p, c_size, c_int, c_void_p, c_void_p, c_void_p]),
+    ("qrc_xchg_create", c_int, [ctypes.POINTER(c_void_p), c_int, c_int, c_int]),
+    ("qrc_xchg_get_handle", c_int, [c_void_p, c_void_p]),
+    ("qrc_xchg_set_peer", c_int, [c_void_p, c_int, c_void_p]),
+    ("qrc_xchg_destroy", c_int, [c_void_p]),
+    ("qrc_absmax_f32_allreduce", c_int, [c_void_p, c_size, c_void_p, c_void_p, c_void_p, c_void_p]),
+    ("qrc_xchg_debug_set_peer_ptr", c_int, [c_void_p, c_int, c_void_p]),
+    ("qrc_xchg_debug_slots", c_void_p, [c_void_p]),
+    ("qrc_xchg_debug_post", c_int, [c_void_p, c_int, ctypes.c_uint32, ctypes.c_uint32]),
+    ("qrc_xchg_epoch", ctypes.c_uint32, [c_void_p]),
     ("qrc_absmax_f32_noalloc", c_int, [c_void_p, c_size, c_void_p, c_void_p]),
     ("qrc_absmax_f32_host", c_int, [c_void_p, c_size, ctypes.POINTER(c_float), c_void_p, c_void_p]),
     ("qrc_amax_quant_e4m3", c_int, [c_void_p, c_size, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),

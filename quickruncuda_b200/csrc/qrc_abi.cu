@@ -33,6 +33,13 @@ qrc_k_absmax_f32(const float* in, qrc_u64 n, qrc_u32* map, float* out, qrc_u32 m
     qrc::reduce_run<qrc::OpAbsF32>(in, n, map, out, nullptr, mode);
 }
 
+// absmax whose last CTA also combines with the other GPUs (qrc_xchg).
+template <int T>
+__global__ void __launch_bounds__(T, 1024 / T)
+qrc_k_absmax_f32_xchg(const float* in, qrc_u64 n, qrc_u32* map, float* out, qrc_u32 mode, qrc::XchgArgs xa) {
+    qrc::reduce_run<qrc::OpAbsF32>(in, n, map, out, nullptr, mode, xa);
+}
+
 // The other operators of qrc_reduce_f32 (absmax keeps its own kernel name).
 template <class Op, int T>
 __global__ void __launch_bounds__(T, 1024 / T)
@@ -400,6 +407,132 @@ QRC_API int qrc_reduce_f32(const float* d_in, size_t n, int op, void* d_out, qrc
     }
 }
 
+// ---------------------------------------------------------------------------
+// Cross-GPU exchange (one rank per GPU)
+// ---------------------------------------------------------------------------
+
+struct qrc_xchg {
+    int device = 0, rank = 0, world = 1;
+    qrc_u64* d_slots = nullptr;             // 2 x world words, zeroed
+    qrc_u64** d_peers = nullptr;            // world pointers, on the device
+    qrc_u64* h_peers[QRC_XCHG_MAX_WORLD] = {};
+    bool opened[QRC_XCHG_MAX_WORLD] = {};   // IPC mappings to close
+    qrc_u32 epoch = 0;
+};
+
+QRC_API int qrc_xchg_create(qrc_xchg** out, int device, int rank, int world) {
+    if (!out || world < 1 || world > QRC_XCHG_MAX_WORLD || rank < 0 || rank >= world) return QRC_ERR_INVALID;
+    *out = nullptr;
+    DeviceScope scope(device);
+    if (!scope.ok) return QRC_ERR_DEVICE;
+    qrc_xchg* x = new qrc_xchg();
+    x->device = device; x->rank = rank; x->world = world;
+    if (cudaMalloc(&x->d_slots, 2 * (size_t)world * sizeof(qrc_u64)) != cudaSuccess ||
+        cudaMalloc(&x->d_peers, (size_t)world * sizeof(qrc_u64*)) != cudaSuccess ||
+        cudaMemset(x->d_slots, 0, 2 * (size_t)world * sizeof(qrc_u64)) != cudaSuccess) {
+        g_last_cuda = (int)cudaGetLastError();
+        if (x->d_slots) cudaFree(x->d_slots);
+        if (x->d_peers) cudaFree(x->d_peers);
+        delete x;
+        return QRC_ERR_CUDA;
+    }
+    x->h_peers[rank] = x->d_slots;
+    *out = x;
+    return QRC_OK;
+}
+
+QRC_API int qrc_xchg_get_handle(const qrc_xchg* x, void* handle) {
+    if (!x || !handle) return QRC_ERR_INVALID;
+    DeviceScope scope(x->device);
+    if (!scope.ok) return QRC_ERR_DEVICE;
+    cudaIpcMemHandle_t h;
+    QRC_CK(cudaIpcGetMemHandle(&h, x->d_slots));
+    static_assert(sizeof(h) == QRC_XCHG_HANDLE_BYTES, "IPC handle size");
+    std::memcpy(handle, &h, sizeof(h));
+    return QRC_OK;
+}
+
+static int xchg_set(qrc_xchg* x, int peer, qrc_u64* p, bool opened) {
+    x->h_peers[peer] = p;
+    x->opened[peer] = opened;
+    QRC_CK(cudaMemcpy(x->d_peers, x->h_peers, (size_t)x->world * sizeof(qrc_u64*), cudaMemcpyHostToDevice));
+    return QRC_OK;
+}
+
+QRC_API int qrc_xchg_set_peer(qrc_xchg* x, int peer, const void* handle) {
+    if (!x || !handle || peer < 0 || peer >= x->world || peer == x->rank || x->h_peers[peer]) return QRC_ERR_INVALID;
+    DeviceScope scope(x->device);
+    if (!scope.ok) return QRC_ERR_DEVICE;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof(h));
+    void* p = nullptr;
+    QRC_CK(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+    return xchg_set(x, peer, (qrc_u64*)p, true);
+}
+
+QRC_API int qrc_xchg_debug_set_peer_ptr(qrc_xchg* x, int peer, void* d_slots) {
+    if (!x || !d_slots || peer < 0 || peer >= x->world || peer == x->rank || x->h_peers[peer]) return QRC_ERR_INVALID;
+    DeviceScope scope(x->device);
+    if (!scope.ok) return QRC_ERR_DEVICE;
+    return xchg_set(x, peer, (qrc_u64*)d_slots, false);
+}
+
+QRC_API void* qrc_xchg_debug_slots(const qrc_xchg* x) { return x ? (void*)x->d_slots : nullptr; }
+
+QRC_API int qrc_xchg_debug_post(qrc_xchg* x, int peer, uint32_t epoch, uint32_t value_bits) {
+    if (!x || peer < 0 || peer >= x->world) return QRC_ERR_INVALID;
+    DeviceScope scope(x->device);
+    if (!scope.ok) return QRC_ERR_DEVICE;
+    const qrc_u64 word = ((qrc_u64)epoch << 32) | value_bits;
+    QRC_CK(cudaMemcpy(x->d_slots + (size_t)(epoch & 1u) * x->world + peer, &word, sizeof(word),
+                      cudaMemcpyHostToDevice));
+    return QRC_OK;
+}
+QRC_API uint32_t qrc_xchg_epoch(const qrc_xchg* x) { return x ? x->epoch : 0u; }
+
+QRC_API int qrc_xchg_destroy(qrc_xchg* x) {
+    if (!x) return QRC_OK;
+    DeviceScope scope(x->device);
+    for (int p = 0; p < x->world; p++)
+        if (x->opened[p]) cudaIpcCloseMemHandle(x->h_peers[p]);
+    if (x->d_slots) cudaFree(x->d_slots);
+    if (x->d_peers) cudaFree(x->d_peers);
+    delete x;
+    return QRC_OK;
+}
+
+QRC_API int qrc_absmax_f32_allreduce(const float* d_in, size_t n, float* d_out, qrc_ctx* c, qrc_xchg* x,
+                                     void* stream) {
+    if (!c || !x || !d_out || (n && !d_in) || ((uintptr_t)d_in & 3)) return QRC_ERR_INVALID;
+    if (x->device != c->device) return QRC_ERR_INVALID;
+    if (n > ((size_t)1 << 61)) return QRC_ERR_RANGE;
+    for (int p = 0; p < x->world; p++)
+        if (!x->h_peers[p]) return QRC_ERR_STATE;            // a peer's slots are not mapped yet
+    DeviceScope scope(c->device);
+    if (!scope.ok) return QRC_ERR_STATE;
+    cudaStream_t s = as_stream(stream);
+    const qrc::XchgArgs xa{x->d_slots, x->d_peers, (qrc_u32)x->rank, (qrc_u32)x->world, ++x->epoch};
+    const int grid = c->num_sms * c->blocks_per_sm;
+    const size_t smem = launch_smem(c);
+    const qrc_u32 mode = (qrc_u32)c->mode;
+    static size_t granted[3] = {0, 0, 0};
+    switch (c->threads) {
+        case 1024:
+            if (smem > granted[0]) { QRC_CK(cudaFuncSetAttribute(qrc_k_absmax_f32_xchg<1024>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)); granted[0] = smem; }
+            QRC_CK(launch(c, qrc_k_absmax_f32_xchg<1024>, grid, 1024, smem, s, d_in, (qrc_u64)n, c->d_map, d_out, mode, xa));
+            break;
+        case 512:
+            if (smem > granted[1]) { QRC_CK(cudaFuncSetAttribute(qrc_k_absmax_f32_xchg<512>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)); granted[1] = smem; }
+            QRC_CK(launch(c, qrc_k_absmax_f32_xchg<512>, grid, 512, smem, s, d_in, (qrc_u64)n, c->d_map, d_out, mode, xa));
+            break;
+        default:
+            if (smem > granted[2]) { QRC_CK(cudaFuncSetAttribute(qrc_k_absmax_f32_xchg<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)); granted[2] = smem; }
+            QRC_CK(launch(c, qrc_k_absmax_f32_xchg<256>, grid, 256, smem, s, d_in, (qrc_u64)n, c->d_map, d_out, mode, xa));
+            break;
+    }
+    return QRC_OK;
+}
+
 QRC_API int qrc_absmax_f32_host(const float* h_in, size_t n, float* h_out, qrc_ctx* c, void* stream) {
     if (!c || !h_out || (n && !h_in)) return QRC_ERR_INVALID;
     DeviceScope scope(c->device);
@@ -546,6 +679,7 @@ QRC_API int qrc_ctx_clear_diagnostics(qrc_ctx* c) {
     DeviceScope scope(c->device);
     QRC_CK(cudaDeviceSynchronize());
     QRC_CK(cudaMemset(c->d_map + qrc::H_ERR, 0, 8 * 4));
+    QRC_CK(cudaMemset(c->d_map + qrc::H_XCHG_ERR, 0, 4));
     return QRC_OK;
 }
 

@@ -177,6 +177,7 @@ enum : qrc_u32 {
     H_ERR = 96, H_ERR_ADDR_LO = 97, H_ERR_ADDR_HI = 98, H_WAIT_ERR = 99,
     H_COV_BYTES_LO = 100, H_COV_BYTES_HI = 101, H_COV_XOR_LO = 102, H_COV_XOR_HI = 103,
     H_ACC64 = 104,                                 // 8-byte aligned double accumulator (sums), 104..105
+    H_XCHG_ERR = 106,                              // a peer's value never arrived (sticky until cleared)
     O_BITLAT = 128,                                // 21 raw latencies of the mask probes
     O_SM_SIDE = 256,                               // per SM: 0 unknown, else 1 + side + 2 * index within side
     O_SM_LAT = 512,                                // per SM raw anchor latency (cycles)
@@ -1156,8 +1157,44 @@ QRC_DEV double block_sum_f64(double v) {
 // How blocks and the grid combine an operator's values (see the element
 // operators): block(), a fire-and-forget global reduction into the map, and
 // the last CTA's take-and-reset of the global accumulator.
+// Cross-GPU combine of the launch's value (see XchgArgs): each rank stores
+// (epoch, value) in its slot of every rank's slot array over NVLink, then
+// waits, bounded, until its own array holds this epoch from every rank.
+struct XchgArgs {
+    qrc_u64* local;                  // this rank's slots: 2 (epoch parity) x world
+    qrc_u64* const* peers;           // every rank's slot array, peers[rank] == local
+    qrc_u32 rank, world, epoch;      // world <= 1: no exchange
+};
+constexpr long long kXchgWaitCycles = 1ll << 32;   // ~2 s at 2 GHz
+
+// Thread 0 of the last CTA: max of `r` over all ranks; false on timeout.
+QRC_DEV bool xchg_max_u32(const XchgArgs& x, qrc_u32& r) {
+    const qrc_u32 par = x.epoch & 1u;
+    const qrc_u64 word = ((qrc_u64)x.epoch << 32) | r;
+    for (qrc_u32 p = 0; p < x.world; p++) {
+        qrc_u64* dst = x.peers[p] + par * x.world + x.rank;
+        asm volatile("st.relaxed.sys.global.u64 [%0], %1;" :: "l"(dst), "l"(word) : "memory");
+    }
+    const long long t0 = clock64();
+    qrc_u32 m = r;
+    for (qrc_u32 q = 0; q < x.world; q++) {
+        qrc_u64 v;
+        for (;;) {
+            asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(x.local + par * x.world + q) : "memory");
+            if ((qrc_u32)(v >> 32) == x.epoch) break;
+            if (clock64() - t0 > kXchgWaitCycles) return false;
+            __nanosleep(256);
+        }
+        const qrc_u32 val = (qrc_u32)v;
+        m = m > val ? m : val;
+    }
+    r = m;
+    return true;
+}
+
 struct FinishMaxU32 {
     typedef qrc_u32 Red;
+    QRC_DEV bool exchange(const XchgArgs& x, Red& r) { return xchg_max_u32(x, r); }
     QRC_DEV Red neutral() { return 0u; }
     QRC_DEV Red block(Red v) { return block_max(v); }
     QRC_DEV Red combine(Red a, Red b) { return a > b ? a : b; }
@@ -1168,6 +1205,7 @@ struct FinishMaxU32 {
 };
 struct FinishSumF64 {
     typedef double Red;
+    QRC_DEV bool exchange(const XchgArgs&, Red&) { return false; }   // not offered for sums
     QRC_DEV Red neutral() { return 0.0; }
     QRC_DEV Red block(Red v) { return block_sum_f64(v); }
     QRC_DEV Red combine(Red a, Red b) { return a + b; }
@@ -1358,7 +1396,8 @@ QRC_DEV typename Op::Acc read_tail(typename Op::Acc acc, const ChunkMap& w, qrc_
 // Bulk pipeline (dynamic shared memory for >= 2 slots per warp): queues only.
 // Mode 3: side-agnostic grid-stride stream.
 template <class Op>
-QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, void* out, float* scale_out, qrc_u32 mode) {
+QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, void* out, float* scale_out, qrc_u32 mode,
+                        XchgArgs xa = XchgArgs{nullptr, nullptr, 0u, 0u, 0u}) {
     typedef typename Op::Finish Fin;
     const qrc_u32 sched = mode & SCHED_MASK;
     mode &= ~SCHED_MASK;
@@ -1592,11 +1631,16 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, void* out, float
     }
     const typename Fin::Red v2 = extra ? Fin::block(Op::to_red(acc2)) : Fin::neutral();
     if (threadIdx.x == 0) {
-        const typename Fin::Red r = Fin::combine(s_acc, v2);
+        typename Fin::Red r = Fin::combine(s_acc, v2);
         map[H_QUEUE0] = 0u;
         map[H_QUEUE1] = 0u;
+        bool err = s_wait_err != 0u;
+        if (xa.world > 1 && !Fin::exchange(xa, r)) {
+            err = true;
+            map[H_XCHG_ERR] = 1u;
+        }
         // a bounded wait that gave up leaves no valid result: NaN
-        Op::publish(out, scale_out, r, s_wait_err != 0u);
+        Op::publish(out, scale_out, r, err);
 #if QRC_TIMELINE
         qrc_u64 t_fin;
         asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_fin));

@@ -2,14 +2,21 @@
 shard with the side-aware kernel, then one single-float max all-reduce.
 
 The reference has no multi-GPU path (QuickRunCUDA.cpp:286 fixes device 0);
-this is the north star's sharded variant.  The exchange is one float per rank,
-so NCCL over NVLink/NVSwitch carries it; max over non-negative, non-NaN floats
-is exact and order-independent, so the result is bit-identical to a
-single-device reduction of the whole stream.
+this is the north star's sharded variant.  The exchange is one float per rank.
+Two ways carry it:
+  * PeerMax: inside the reduction kernel.  The last CTA of each rank stores
+    its partial in every rank's exchange slots over NVLink (CUDA IPC
+    mappings) and waits, bounded, for everyone's (qrc_absmax_f32_allreduce);
+  * combine_max: an NCCL max all-reduce after the kernel.
+Max over non-negative, non-NaN floats is exact and order-independent, so both
+are bit-identical to a single-device reduction of the whole stream.
 """
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
+
+from . import _native as nat
 
 
 @dataclass(frozen=True)
@@ -53,3 +60,65 @@ def sharded_absmax(ctx, shard, out, group=None):
     ctx.absmax(shard, out=out)
     combine_max(out, group)
     return out
+
+
+class PeerMax:
+    """Cross-GPU maximum taken inside the reduction kernel (qrc_xchg).  Built
+    collectively: every rank of `group` must construct it, call `absmax` the
+    same number of times in the same order, and `close` it."""
+
+    def __init__(self, ctx, group=None):
+        import torch.distributed as dist
+        self.ctx, self.lib, self.group = ctx, ctx.lib, group
+        self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+        h = ctypes.c_void_p()
+        nat.check(self.lib, "qrc_xchg_create", self.lib.qrc_xchg_create(ctypes.byref(h), ctx.device, self.rank,
+                                                                       self.world))
+        self._h = h
+        buf = ctypes.create_string_buffer(64)
+        nat.check(self.lib, "qrc_xchg_get_handle", self.lib.qrc_xchg_get_handle(h, buf))
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(buf.raw), group=group)
+        for p in range(self.world):
+            if p != self.rank:
+                nat.check(self.lib, "qrc_xchg_set_peer", self.lib.qrc_xchg_set_peer(h, p, handles[p]))
+
+    @classmethod
+    def try_create(cls, ctx, group=None):
+        """A PeerMax on every rank, or None on every rank when any rank could
+        not map its peers (the caller then uses combine_max)."""
+        import torch.distributed as dist
+        px, ok = None, True
+        try:
+            px = cls(ctx, group)
+        except Exception:
+            ok = False
+        oks = [None] * dist.get_world_size(group)
+        dist.all_gather_object(oks, ok, group=group)
+        if all(oks):
+            return px
+        if px is not None:
+            px.close(barrier=False)
+        return None
+
+    def absmax(self, x, out, n=None, stream=None):
+        """max |x| over every rank's x, into `out` on every rank.  NaN when a
+        peer's value did not arrive within the bounded wait."""
+        from .api import _ptr, _stream_handle
+        n = int(x.numel()) if n is None else n
+        nat.check(self.lib, "qrc_absmax_f32_allreduce",
+                  self.lib.qrc_absmax_f32_allreduce(_ptr(x) or None, n, _ptr(out), self.ctx.handle, self._h,
+                                                    _stream_handle(stream, self.ctx.device) or None))
+        return out
+
+    def close(self, barrier: bool = True) -> None:
+        """Collective: waits until every rank is done before the slots go."""
+        if getattr(self, "_h", None) is None:
+            return
+        import torch
+        torch.cuda.synchronize(self.ctx.device)
+        if barrier:
+            import torch.distributed as dist
+            dist.barrier(group=self.group)
+        self.lib.qrc_xchg_destroy(self._h)
+        self._h = None
