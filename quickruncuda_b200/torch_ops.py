@@ -1,5 +1,5 @@
-"""PyTorch custom operators over the C ABI: `torch.ops.qrc.absmax` and
-`torch.ops.qrc.amax_quant_e4m3`.
+"""PyTorch custom operators over the C ABI: `torch.ops.qrc.absmax`,
+`torch.ops.qrc.reduce` and `torch.ops.qrc.amax_quant_e4m3`.
 
 These are for callers that hold tensors rather than raw buffers, such as a
 quantized-inference stack computing per-tensor FP8 scales.  They are opaque
@@ -79,6 +79,30 @@ def absmax(x: torch.Tensor) -> torch.Tensor:
 @absmax.register_fake
 def _(x: torch.Tensor) -> torch.Tensor:
     return x.new_empty((), dtype=torch.float32)
+
+
+_REDUCE_DTYPES = {"absmax": torch.float32, "max": torch.float32, "min": torch.float32,
+                  "sum": torch.float64, "sumsq": torch.float64}
+
+
+@torch.library.custom_op("qrc::reduce", mutates_args=(), device_types="cuda")
+def reduce(x: torch.Tensor, op: str) -> torch.Tensor:
+    """Side-aware reduction of a float32 CUDA tensor: op 'absmax', 'max',
+    'min' (0-dim float32, NaN elements skipped) or 'sum', 'sumsq' (0-dim
+    float64, accumulated in double)."""
+    _check_cuda(x, (torch.float32,), "reduce")
+    if op not in _REDUCE_DTYPES:
+        raise RuntimeError(f"qrc::reduce: unknown op {op!r}")
+    ctx = _context_for(x)
+    out = ctx.reduce(x, op, stream=torch.cuda.current_stream(x.device))
+    return out.view(())
+
+
+@reduce.register_fake
+def _(x: torch.Tensor, op: str) -> torch.Tensor:
+    if op not in _REDUCE_DTYPES:
+        raise RuntimeError(f"qrc::reduce: unknown op {op!r}")
+    return x.new_empty((), dtype=_REDUCE_DTYPES[op])
 
 
 @torch.library.custom_op("qrc::amax_quant_e4m3", mutates_args=(), device_types="cuda")

@@ -12,6 +12,7 @@ from torch._subclasses.fake_tensor import FakeTensorMode
 def test_registered():
     assert hasattr(torch.ops.qrc, "absmax")
     assert hasattr(torch.ops.qrc, "amax_quant_e4m3")
+    assert hasattr(torch.ops.qrc, "reduce")
 
 
 @pytest.mark.parametrize("shape", [(0,), (7,), (3, 5), (2, 3, 4)])
@@ -20,6 +21,8 @@ def test_fake_shapes(shape):
         x = torch.empty(shape, device="cuda")
         y = torch.ops.qrc.absmax(x)
         assert y.shape == () and y.dtype == torch.float32 and y.device.type == "cuda"
+        assert torch.ops.qrc.reduce(x, "sum").dtype == torch.float64
+        assert torch.ops.qrc.reduce(x, "min").dtype == torch.float32
         xb = torch.empty(shape, device="cuda", dtype=torch.bfloat16)
         q, scale, amax = torch.ops.qrc.amax_quant_e4m3(xb)
         assert q.shape == xb.shape and q.dtype == torch.float8_e4m3fn

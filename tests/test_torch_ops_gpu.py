@@ -70,3 +70,20 @@ def test_ops_inside_torch_compile(cuda, qrc, oracle):
     assert _bits(a) == _bits(a0) == oracle.absmax_bits((x * 2.0).cpu().numpy())
     assert torch.equal(q.view(torch.uint8), q0.view(torch.uint8)) and s.item() == s0.item()
     ops.clear_context_cache()
+
+
+def test_reduce_op_matches_oracle(cuda, qrc, oracle):
+    import torch
+    import quickruncuda_b200.torch_ops as ops
+    x = torch.empty((1 << 21) + 9, dtype=torch.float32, device=cuda)
+    qrc.fill_normal(x, seed=4, sigma=2.0)
+    host = x.cpu().numpy()
+    for op in ("max", "min"):
+        got = torch.ops.qrc.reduce(x, op)
+        assert got.dtype == torch.float32 and np.float32(got.item()) == oracle.reduce(op, host)
+    for op in ("sum", "sumsq"):
+        got = torch.ops.qrc.reduce(x, op)
+        want, abs_sum = oracle.reduce(op, host)
+        assert got.dtype == torch.float64
+        assert abs(got.item() - want) <= host.size * 2.0 ** -52 * abs_sum
+    ops.clear_context_cache()
