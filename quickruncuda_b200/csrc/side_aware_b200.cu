@@ -88,8 +88,8 @@ constexpr int kProbeIters = 32;                  // dependent atomics per latenc
 constexpr int kMaxSm = 256;
 // Compile-time knobs (a kernel-file user can set them with the harness' -H,
 // like the reference's own #defines):
-//   QRC_MAX_GRAB   most pairs a warp takes per queue atomic (guided: grabs
-//                  shrink to 1 pair as its side's queue empties)
+//   QRC_MAX_GRAB   queue schedule: most pairs a warp takes per queue atomic
+//                  (guided: grabs shrink to 1 pair as its side's queue empties)
 //   QRC_LOAD_KIND  0 ld.global.v4, 1 ld.global.nc.L1::no_allocate.L2::256B.v4,
 //                  2 as 1 plus L2::evict_first, 3 256-bit ld.global.nc.v8,
 //                  4 ld.global.nc.L1::no_allocate.v4 (no L2 prefetch size)
@@ -121,8 +121,9 @@ constexpr int kMaxSm = 256;
 #ifndef QRC_FINISH
 #define QRC_FINISH 1
 #endif
-//   QRC_SHARES     1: static per-SM shares for 7/8 of the pairs (see
-//                  reduce_run); 0: every pair through the side queues
+//   QRC_SHARES     1: the static and balanced schedules may use static
+//                  per-SM shares (see reduce_run); 0: every pair goes through
+//                  the side queues
 #ifndef QRC_SHARES
 #define QRC_SHARES 1
 #endif
