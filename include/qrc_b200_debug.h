@@ -38,6 +38,11 @@ int qrc_debug_cvt_e4m3(const float* d_in, size_t n, uint8_t* d_out, void* stream
  * from a test on the same scratch). */
 void* qrc_ctx_map_device_ptr(const struct qrc_ctx* ctx);
 
+/* 1 (default): the quantize's second pass reads side-aware when the input is
+ * inside the context's mapped buffer and aligned; 0: always the side-agnostic
+ * pass (for comparing the two). */
+int qrc_ctx_debug_quant_side_aware(struct qrc_ctx* ctx, int enable);
+
 /* Exchange tests on one GPU: map a peer's slot array to a local device buffer
  * (no IPC), read this rank's slot array, and the epoch of the last launch.
  * With them a test can play a peer from the host (write its slot before the

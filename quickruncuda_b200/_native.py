@@ -76,6 +76,7 @@ SIGNATURES = [
     ("qrc_absmax_f32_allreduce", c_int, [c_void_p, c_size, c_void_p, c_void_p, c_void_p, c_void_p]),
     ("qrc_xchg_debug_set_peer_ptr", c_int, [c_void_p, c_int, c_void_p]),
     ("qrc_xchg_debug_slots", c_void_p, [c_void_p]),
+    ("qrc_ctx_debug_quant_side_aware", c_int, [c_void_p, c_int]),
     ("qrc_xchg_debug_post", c_int, [c_void_p, c_int, ctypes.c_uint32, ctypes.c_uint32]),
     ("qrc_xchg_epoch", ctypes.c_uint32, [c_void_p]),
     ("qrc_absmax_f32_noalloc", c_int, [c_void_p, c_size, c_void_p, c_void_p]),

@@ -179,6 +179,7 @@ enum : qrc_u32 {
     H_COV_BYTES_LO = 100, H_COV_BYTES_HI = 101, H_COV_XOR_LO = 102, H_COV_XOR_HI = 103,
     H_ACC64 = 104,                                 // 8-byte aligned double accumulator (sums), 104..105
     H_XCHG_ERR = 106,                              // a peer's value never arrived (sticky until cleared)
+    H_QUANT_TICKET = 107,                          // side-aware quantize pass: CTAs done
     O_BITLAT = 128,                                // 21 raw latencies of the mask probes
     O_SM_SIDE = 256,                               // per SM: 0 unknown, else 1 + side + 2 * index within side
     O_SM_LAT = 512,                                // per SM raw anchor latency (cycles)

@@ -106,3 +106,31 @@ def test_e4m3_conversion_exhaustive(cuda, qrc, oracle):
         bad = np.nonzero(got != want)[0]
         assert bad.size == 0, [(hex(first + int(i)), hex(got[i]), hex(want[i])) for i in bad[:8]]
         del bits, xs
+
+
+@pytest.mark.parametrize("mode", [0, 1, 2])
+def test_side_aware_quant_pass_on_mapped_buffer(cuda, qrc, oracle, mode):
+    """The second pass reads side-aware when the input lies in the context's
+    buffer: sizes and 16-byte-aligned offsets that give partial blocks, a
+    head and a tail, against the oracle and the side-agnostic pass."""
+    import torch
+    total = (1 << 22) + 4096
+    base = oracle.normal_bf16(6, total, sigma=2.0)
+    xb = _bf16_tensor(cuda, base)
+    with qrc.SideAwareContext(xb) as ctx:
+        assert ctx.info["status"] == 0
+        ctx.mode = mode
+        for off, n in [(0, total), (8, total - 8), (4096, 1 << 22), (8, 8191), (0, 8), (24, (1 << 21) + 5)]:
+            view = xb[off:off + n]
+            q1, s1, a1 = ctx.amax_quant_e4m3(view)
+            qo, so = oracle.amax_quant_e4m3(base[off:off + n])
+            assert np.float32(s1.item()) == so
+            assert np.array_equal(q1.cpu().numpy(), qo), (mode, off, n)
+            assert ctx.lib.qrc_ctx_debug_quant_side_aware(ctx.handle, 0) == 0
+            q2, s2, _ = ctx.amax_quant_e4m3(view)
+            assert ctx.lib.qrc_ctx_debug_quant_side_aware(ctx.handle, 1) == 0
+            assert torch.equal(q1, q2) and s1.item() == s2.item()
+        # back-to-back launches: each pass leaves the queues reset
+        for _ in range(3):
+            q3, _, _ = ctx.amax_quant_e4m3(xb)
+        assert np.array_equal(q3.cpu().numpy(), oracle.amax_quant_e4m3(base)[0])
