@@ -1243,8 +1243,13 @@ QRC_DEV qrc_u32 block_page_word(const ChunkMap& w, const Shares& sh, qrc_u64 b) 
     const qrc_u64 pg = (w.lo + (b << 16) - w.page_base) >> 21;
     return w.page_bits[pg >> 5];
 }
-QRC_DEV qrc_u32 share_first_page_word(const ChunkMap& w, const Shares& sh, int k) {
-    return block_page_word(w, sh, (qrc_u64)k * (blockDim.x >> 8) + (threadIdx.x >> 8));
+// `word0` is page-bit word 0, loaded with the map header: a share whose first
+// block lies in the first 64 MiB of the mapped buffer needs no second load.
+QRC_DEV qrc_u32 share_first_page_word(const ChunkMap& w, const Shares& sh, int k, qrc_u32 word0) {
+    const qrc_u64 b = (qrc_u64)k * (blockDim.x >> 8) + (threadIdx.x >> 8);
+    if (!w.use_page_bits || (w.lo & 0xFFFFull) != 0 || (b + 1) * 8 > sh.R) return 0u;
+    const qrc_u64 pg = (w.lo + (b << 16) - w.page_base) >> 21;
+    return (pg >> 5) == 0 ? word0 : w.page_bits[pg >> 5];
 }
 
 // `pw` is share_first_page_word(w, sh, k).
@@ -1440,6 +1445,7 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, void* out, float
     } else {
         ChunkMap cm;
         cm.setup(a, end, map, mode);      // reads only the map header, which reductions never write
+        const qrc_u32 word0 = map[O_PAGE_BITS];   // goes out with the header loads
         lo = cm.lo; hi = cm.hi;
         const int S = bulk_slots_per_warp(dynamic_smem_size(), W);
         sh.on = QRC_SHARES && cm.aware && S < 2 && cm.C == 4096 && (blockDim.x & 255) == 0 &&
@@ -1456,7 +1462,7 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, void* out, float
         }
         const int own_k = cm.sm_index;
         const bool own_share = sh.on && own_k >= 0 && (qrc_u32)own_k < sh.sms(cm.side);
-        const qrc_u32 pw0 = own_share ? share_first_page_word(cm, sh, own_k) : 0u;
+        const qrc_u32 pw0 = own_share ? share_first_page_word(cm, sh, own_k, word0) : 0u;
         griddep_wait();                   // the scratch of the previous launch is reset
 #if QRC_TIMELINE
         qrc_u64 t_start;
@@ -1621,8 +1627,8 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, void* out, float
             extra = true;
             ChunkMap cm;                      // only when a share was missed
             cm.setup(a, end, map, mode);
-            acc2 = read_share<Op>(acc2, cm, sh, pick >> 7, pick & 127, share_first_page_word(cm, sh, pick & 127)
-                                  QRC_CS_ARG);
+            acc2 = read_share<Op>(acc2, cm, sh, pick >> 7, pick & 127,
+                                  share_first_page_word(cm, sh, pick & 127, cm.page_bits[0]) QRC_CS_ARG);
         }
         for (int i = threadIdx.x; i < 256; i += blockDim.x) map[O_CLAIMS + i] = 0u;
 #ifdef QRC_CHECKED
