@@ -180,11 +180,12 @@ enum : qrc_u32 {
     H_ACC64 = 104,                                 // 8-byte aligned double accumulator (sums), 104..105
     H_XCHG_ERR = 106,                              // a peer's value never arrived (sticky until cleared)
     H_QUANT_TICKET = 107,                          // side-aware quantize pass: CTAs done
+    H_EPOCH = 108,                                 // share-mark tag of the last launch with shares
     O_BITLAT = 128,                                // 21 raw latencies of the mask probes
     O_SM_SIDE = 256,                               // per SM: 0 unknown, else 1 + side + 2 * index within side
     O_SM_LAT = 512,                                // per SM raw anchor latency (cycles)
     O_PAGE_LAT = 1024,                             // first kDiagPages raw page latencies
-    O_CLAIMS = 2048,                               // share marks: side * 128 + index within side
+    O_CLAIMS = 2048,                               // share marks (launch tags): side * 128 + index within side
     O_TIMELINE = 3072,                             // QRC_TIMELINE: 4 words per CTA, 256 CTAs
     O_PAGE_BITS = 4096,                            // one bit per 2 MiB page
 };
@@ -1419,6 +1420,8 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, void* out, float
 #endif
     qrc_u64 lo, hi;   // body [lo, hi); edges [a, lo) and [hi, end)
     Shares sh;
+    __shared__ qrc_u32 s_tag;                        // this launch's share-mark tag (share path)
+    __shared__ qrc_u32 s_mark;                       // map word of this CTA's share mark, 0 if none
     sh.on = false;
     sh.K0 = sh.K1 = 0;
 
@@ -1473,23 +1476,31 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, void* out, float
 #endif
         if (sh.on) {
             // The tail's first claim goes out now; only its reply stays live
-            // while the share is read.
+            // while the share is read.  A share's mark holds the tag of the
+            // launch that read it (last launch's tag + 1), so marks need no
+            // reset between launches.
             const bool tail = cm.npairs > sh.R;
             qrc_u32 first = 0;
             if (tail && (threadIdx.x & 255) == 0) first = atomicAdd(&map[cm.side ? H_QUEUE1 : H_QUEUE0], 1u);
+            // The last warp fetches the tag (it alone waits for the reply);
+            // the finish, after its barriers, writes the mark.
+            if (threadIdx.x == blockDim.x - 32) s_tag = __ldcg(&map[H_EPOCH]) + 1u;
+            if (threadIdx.x == 0) s_mark = own_share ? O_CLAIMS + 128 * cm.side + own_k : 0u;
             if (own_share) {
                 if constexpr (Op::kIdempotent) {
                     // two CTAs on one SM both read the share: harmless
-                    if (threadIdx.x == 0) *(volatile qrc_u32*)&map[O_CLAIMS + 128 * cm.side + own_k] = 1u;
                     acc = plain ? read_share<Op, 0>(acc, cm, sh, cm.side, own_k, pw0 QRC_CS_ARG)
                                 : read_share<Op>(acc, cm, sh, cm.side, own_k, pw0 QRC_CS_ARG);
                 } else {
                     // Exactly once: the first CTA to set the mark owns the
-                    // share.  The share is read into its own accumulator
-                    // while the claim is in flight, and dropped if it lost.
+                    // share.  Warp 0 waits for the claim; the other warps
+                    // read the share into its own accumulator meanwhile, and
+                    // it is dropped if the claim was lost.
                     __shared__ qrc_u32 s_lost;
-                    qrc_u32 old = 0;
-                    if (threadIdx.x == 0) old = atomicExch(&map[O_CLAIMS + 128 * cm.side + own_k], 1u);
+                    if (threadIdx.x == 0) {
+                        const qrc_u32 tag = __ldcg(&map[H_EPOCH]) + 1u;
+                        s_lost = atomicExch(&map[O_CLAIMS + 128 * cm.side + own_k], tag) == tag;
+                    }
 #ifdef QRC_CHECKED
                     // coverage counts only the reads whose values are kept
                     CheckState cs_all = cs;
@@ -1497,8 +1508,7 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, void* out, float
 #endif
                     typename Op::Acc part = plain ? read_share<Op, 0>(Op::zero(), cm, sh, cm.side, own_k, pw0 QRC_CS_ARG)
                                                   : read_share<Op>(Op::zero(), cm, sh, cm.side, own_k, pw0 QRC_CS_ARG);
-                    if (threadIdx.x == 0) s_lost = old;
-                    __syncthreads();
+                    __syncthreads();                              // s_lost: another CTA of this launch had it
                     if (!s_lost) acc = Op::merge(acc, part);
 #ifdef QRC_CHECKED
                     if (s_lost) { cs.bytes = cs_all.bytes; cs.xr = cs_all.xr; }
@@ -1571,6 +1581,7 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, void* out, float
     __shared__ int s_last;
     if (threadIdx.x == 0) {
         qrc_u32 t;
+        if (Op::kIdempotent && sh.on && s_mark) map[s_mark] = s_tag;   // ordered before the ticket
 #if QRC_FINISH == 1
         // The block's value goes out as a fire-and-forget reduction; the
         // ticket increment has release semantics (ordered after it) and
@@ -1591,12 +1602,13 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, void* out, float
     if (!s_last) return;
 
     // ---- last CTA: unmarked shares, then publish ---------------------------
-    // Thread 0 takes the accumulator while warp 0 checks the share marks, in
-    // the same round trip; only a missing share costs more.
+    // Warp 1 takes the accumulator while warp 0 loads the share marks: one
+    // round trip for both (the same warp would stall on the exchange's reply
+    // before issuing the mark loads).  Only a missing share costs more.
     __shared__ typename Fin::Red s_acc;
     __shared__ qrc_u32 s_wait_err;
     __shared__ int s_share;
-    if (threadIdx.x == 0) {
+    if (threadIdx.x == (blockDim.x > 32 ? 32u : 0u)) {
         s_acc = Fin::take(map);
         s_wait_err = __ldcg(&map[H_WAIT_ERR]);
     }
@@ -1612,12 +1624,12 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, void* out, float
                 #pragma unroll
                 for (int t = 7; t >= 0; t--) {
                     const int k = (32 * t + lane) & 127;
-                    const unsigned m = __ballot_sync(0xFFFFFFFFu, (qrc_u32)k < sh.sms(t >> 2) && mark[t] == 0u);
+                    const unsigned m = __ballot_sync(0xFFFFFFFFu, (qrc_u32)k < sh.sms(t >> 2) && mark[t] != s_tag);
                     if (m) found = 32 * t + __ffs(m) - 1;
                 }
                 if (lane == 0) {
                     s_share = found;
-                    if (found >= 0) map[O_CLAIMS + found] = 1u;
+                    if (found >= 0) map[O_CLAIMS + found] = s_tag;
                 }
             }
             __syncthreads();
@@ -1630,7 +1642,7 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, void* out, float
             acc2 = read_share<Op>(acc2, cm, sh, pick >> 7, pick & 127,
                                   share_first_page_word(cm, sh, pick & 127, cm.page_bits[0]) QRC_CS_ARG);
         }
-        for (int i = threadIdx.x; i < 256; i += blockDim.x) map[O_CLAIMS + i] = 0u;
+        if (threadIdx.x == 0) map[H_EPOCH] = s_tag;      // the next launch marks with s_tag + 1
 #ifdef QRC_CHECKED
         cov_flush(cs, lane, map);
 #endif
