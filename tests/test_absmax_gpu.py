@@ -287,3 +287,24 @@ def test_full_size_config2(cuda, qrc, oracle):
             assert _bits(ctx.absmax(x)) == want
     del x
     torch.cuda.empty_cache()
+
+
+def test_beyond_2_pow_32_elements(cuda, qrc):
+    """17 GB: element indices past 2^32 (64-bit address arithmetic in the
+    walks and the tail), every schedule; the planted outlier is the answer."""
+    import torch
+    n = (1 << 32) + 3
+    x = torch.empty(n, dtype=torch.float32, device=cuda)
+    qrc.fill_uniform(x, seed=17)
+    try:
+        with qrc.SideAwareContext(x) as ctx:
+            for pos, val in [((1 << 32) + 1, -9.5), (n - 1, 11.25), (123, 3.0)]:
+                old = float(x[pos].item())
+                x[pos] = val
+                for mode in (0, 0x10, 0x20, 0x30, 3):
+                    ctx.mode = mode
+                    assert ctx.absmax(x).item() == abs(val), (mode, pos)
+                x[pos] = old
+    finally:
+        del x
+        torch.cuda.empty_cache()

@@ -113,3 +113,13 @@ def test_reference_known_answer_999(tmp_path):
     res = harness_json(["--cubin", REF_CUBIN_999, "-i", "-p", "-t", "1024", "-A", n, "-0", n, "-C", 1,
                         "-T", 2, "--fill-a", "uniform:2"], tmp_path)
     assert res["c0"] == 999.0
+
+
+def test_kernel_file_at_the_plugin_int_limit(tmp_path):
+    """n = 2^31 - 1 floats (8.6 GB), the largest `-0` the plugin's int
+    argument can carry (tests/side_aware.cu:257): the planted outlier is the
+    result."""
+    n = (1 << 31) - 1
+    res = harness_json(["-i", "-p", "-t", "1024", "-A", n, "-0", n, "-C", 1, "-T", 2,
+                        "--fill-a", "uniform:5:7.5", KERNEL_FILE], tmp_path)
+    assert res["c0"] == 7.5
