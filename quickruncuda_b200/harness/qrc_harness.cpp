@@ -19,13 +19,22 @@
 //     QuickRunCUDA.cpp:291, utils/nvmlClass.h:275-302);
 //   * --json prints one JSON object with the measurements;
 //   * --dump-b FILE writes buffer B raw after the runs (kernel-file state);
-//   * --clock-speed and --server are not provided: this harness changes no
-//     GPU setting and is a one-shot process.
+//   * --clock-speed is not provided: this harness changes no GPU setting;
+//   * --server [--server-dir D] keeps one process (and its CUDA context)
+//     alive and runs command lines written to the FIFO D/quickruncuda_cmd
+//     (D = /tmp by default, the reference's path), answering with the
+//     command's standard output on D/quickruncuda_resp
+//     (QuickRunCUDA.cpp:298-343, utils/ipc_helper.h).  "exit" ends it.  A
+//     failing command answers with its error instead of ending the server,
+//     and every command frees what it allocated.
 // Errors print a message and exit non-zero (the reference exits from
 // checkCudaErrors, utils/cuda_helper.h:17-33).
 #include <cuda.h>
 #include <nvrtc.h>
 #include <nvml.h>
+#include <fcntl.h>
+#include <sys/stat.h>
+#include <unistd.h>
 
 #include <algorithm>
 #include <atomic>
@@ -86,9 +95,14 @@ bool load_nvml() {
 
 namespace {
 
-[[noreturn]] void die(const std::string& msg) {
+// In server mode an error ends the command, not the process.
+bool g_server = false;
+struct CommandError { std::string msg; int code; };
+
+[[noreturn]] void die(const std::string& msg, int code = 2) {
+    if (g_server) throw CommandError{msg, code};
     fprintf(stderr, "error: %s\n", msg.c_str());
-    exit(2);
+    exit(code);
 }
 
 void ck(CUresult r, const char* what) {
@@ -125,6 +139,8 @@ struct Args {
     std::string fillA;
     double powerSeconds = 0.0;
     int device = 0;
+    bool server = false;
+    std::string serverDir = "/tmp";
 };
 
 void usage() {
@@ -144,7 +160,8 @@ void usage() {
         "  --dump-c F   --dump-c-format raw|int_csv|float_csv   --load-c F   --dump-b F\n"
         "  --reference-c F   --compare-tolerance X\n"
         "  --fill-a uniform:SEED[:OUTLIER] | normal:SEED[:SIGMA]\n"
-        "  --power-seconds S   --json   --device N\n");
+        "  --power-seconds S   --json   --device N\n"
+        "  --server [--server-dir D]   (commands on D/quickruncuda_cmd, output on D/quickruncuda_resp)\n");
 }
 
 unsigned long long parse_u64(const std::string& s) {
@@ -164,7 +181,7 @@ Args parse(int argc, char** argv) {
     };
     for (int i = 1; i < argc; i++) {
         std::string f = argv[i];
-        if (f == "-h" || f == "--help") { usage(); exit(0); }
+        if (f == "-h" || f == "--help") { usage(); if (g_server) die("", 0); exit(0); }
         else if (f == "-t" || f == "--threadsPerBlock") a.threads = std::stoi(need(i));
         else if (f == "-b" || f == "--blocksPerGrid") a.blocks = std::stoi(need(i));
         else if (f == "-p" || f == "--persistentBlocks") a.persistent = true;
@@ -204,8 +221,10 @@ Args parse(int argc, char** argv) {
         else if (f == "--power-seconds") a.powerSeconds = std::stod(need(i));
         else if (f == "--json") a.json = true;
         else if (f == "--device") a.device = std::stoi(need(i));
-        else if (f == "--clock-speed" || f == "--server")
-            die(f + " is not supported: this harness changes no GPU setting and runs one test per process");
+        else if (f == "--clock-speed")
+            die(f + " is not supported: this harness changes no GPU setting");
+        else if (f == "--server") a.server = true;
+        else if (f == "--server-dir") a.serverDir = need(i);
         else if (!f.empty() && f[0] == '-' && f.size() > 1) die("unknown option " + f);
         else pos.push_back(f);
     }
@@ -350,11 +369,26 @@ struct PowerSampler {
     }
 };
 
-}  // namespace
 
-int main(int argc, char** argv) {
-    Args a = parse(argc, argv);
+// Releases what one run allocated, also when an error ends it early.
+struct RunResources {
+    CUdeviceptr dA = 0, dB = 0, dC = 0, dFlush = 0;
+    CUmodule mod = nullptr;
+    CUdevice dev = 0;
+    bool ctx = false;
+    ~RunResources() {
+        if (!ctx) return;
+        dyn::p_cuCtxSynchronize();
+        if (dA) dyn::p_cuMemFree(dA);
+        if (dB) dyn::p_cuMemFree(dB);
+        if (dC) dyn::p_cuMemFree(dC);
+        if (dFlush) dyn::p_cuMemFree(dFlush);
+        if (mod) dyn::p_cuModuleUnload(mod);
+        dyn::p_cuDevicePrimaryCtxRelease(dev);
+    }
+};
 
+int run_once(Args a) {
     if (a.compileOnly) {
         std::vector<char> cubin = compile_cubin(a);
         printf("compiled %s for %s: %zu bytes\n", a.kernelFile.c_str(), a.arch.c_str(), cubin.size());
@@ -363,14 +397,19 @@ int main(int argc, char** argv) {
 
     if (!dyn::load_driver()) die("cannot load libcuda.so.1 (no GPU driver on this machine)");
     ck(dyn::p_cuInit(0), "cuInit");
-    CUdevice dev;
+    RunResources res;
+    CUdevice& dev = res.dev;
     ck(dyn::p_cuDeviceGet(&dev, a.device), "cuDeviceGet");
     CUcontext ctx;
     ck(dyn::p_cuDevicePrimaryCtxRetain(&ctx, dev), "cuDevicePrimaryCtxRetain");
+    res.ctx = true;
     ck(dyn::p_cuCtxSetCurrent(ctx), "cuCtxSetCurrent");
 
     const size_t sizeA = a.dwordsA * 4, sizeB = a.dwordsB * 4, sizeC = a.dwordsC * 4;
-    CUdeviceptr dA = 0, dB = 0, dC = 0, dFlush = 0;
+    CUdeviceptr& dA = res.dA;
+    CUdeviceptr& dB = res.dB;
+    CUdeviceptr& dC = res.dC;
+    CUdeviceptr& dFlush = res.dFlush;
     ck(dyn::p_cuMemAlloc(&dA, std::max<size_t>(sizeA, 4)), "cuMemAlloc A");
     ck(dyn::p_cuMemAlloc(&dB, std::max<size_t>(sizeB, 4)), "cuMemAlloc B");
     ck(dyn::p_cuMemAlloc(&dC, std::max<size_t>(sizeC, 4)), "cuMemAlloc C");
@@ -391,7 +430,7 @@ int main(int argc, char** argv) {
         std::ofstream o("output.cubin", std::ios::binary);
         if (o) o.write(cubin.data(), (std::streamsize)cubin.size());
     }
-    CUmodule mod;
+    CUmodule& mod = res.mod;
     ck(dyn::p_cuModuleLoadData(&mod, cubin.data()), "cuModuleLoadData");
     CUfunction kfn, ifn = nullptr;
     ck(dyn::p_cuModuleGetFunction(&kfn, mod, "kernel"), "dyn::p_cuModuleGetFunction(kernel)");
@@ -598,9 +637,114 @@ int main(int argc, char** argv) {
                powerW, powerPerf, powerMs, powerClock, powerSamples);
     }
 
-    dyn::p_cuMemFree(dA); dyn::p_cuMemFree(dB); dyn::p_cuMemFree(dC);
-    if (dFlush) dyn::p_cuMemFree(dFlush);
-    dyn::p_cuModuleUnload(mod);
-    dyn::p_cuDevicePrimaryCtxRelease(dev);
-    return status;
+    return status;                  // res frees the buffers and the module
+}
+
+// ---------------------------------------------------------------------------
+// Server mode (QuickRunCUDA.cpp:298-343, utils/ipc_helper.h)
+// ---------------------------------------------------------------------------
+
+// A command line split on white space, with '...' grouping as in the
+// reference's parseCommandString (QuickRunCUDA.cpp:198-240).
+std::vector<std::string> split_command(const std::string& cmd) {
+    std::vector<std::string> out{"qrc_harness"};
+    std::string cur;
+    bool quoted = false, have = false;
+    for (char c : cmd) {
+        if (c == '\'') {
+            if (quoted) { out.push_back(cur); cur.clear(); have = false; }
+            quoted = !quoted;
+        } else if (quoted || !std::isspace((unsigned char)c)) {
+            cur += c; have = true;
+        } else if (have) {
+            out.push_back(cur); cur.clear(); have = false;
+        }
+    }
+    if (have) out.push_back(cur);
+    return out;
+}
+
+std::string read_all(int fd) {
+    std::string s;
+    char buf[65536];
+    ssize_t n;
+    while ((n = read(fd, buf, sizeof(buf))) > 0) s.append(buf, (size_t)n);
+    return s;
+}
+
+// Runs one command with stdout going to a temporary file (no pipe, so large
+// outputs cannot block), and returns that output.
+std::string run_captured(const std::string& cmd) {
+    fflush(stdout);
+    FILE* tmp = tmpfile();
+    if (!tmp) return "error: cannot create a capture file\n";
+    const int saved = dup(STDOUT_FILENO);
+    dup2(fileno(tmp), STDOUT_FILENO);
+    std::string err;
+    try {
+        std::vector<std::string> words = split_command(cmd);
+        std::vector<char*> argv;
+        for (auto& w : words) argv.push_back(&w[0]);
+        Args a = parse((int)argv.size(), argv.data());
+        if (a.server) die("--server inside a server command");
+        run_once(a);
+    } catch (const CommandError& e) {
+        if (!e.msg.empty()) err = "error: " + e.msg + "\n";
+    } catch (const std::exception& e) {
+        err = std::string("error: ") + e.what() + "\n";
+    }
+    fflush(stdout);
+    dup2(saved, STDOUT_FILENO);
+    close(saved);
+    std::string out;
+    rewind(tmp);
+    out = read_all(fileno(tmp));
+    fclose(tmp);
+    return out + err;
+}
+
+int serve(const Args& a) {
+    g_server = true;
+    const std::string cmdPath = a.serverDir + "/quickruncuda_cmd", respPath = a.serverDir + "/quickruncuda_resp";
+    for (const auto& p : {cmdPath, respPath})
+        if (mkfifo(p.c_str(), 0666) != 0 && errno != EEXIST) {
+            fprintf(stderr, "error: cannot create %s: %s\n", p.c_str(), strerror(errno));
+            return 2;
+        }
+    // Keep the primary context alive between commands when a GPU is present.
+    CUdevice dev = 0;
+    CUcontext ctx = nullptr;
+    const bool gpu = dyn::load_driver() && dyn::p_cuInit(0) == CUDA_SUCCESS &&
+                     dyn::p_cuDeviceGet(&dev, a.device) == CUDA_SUCCESS &&
+                     dyn::p_cuDevicePrimaryCtxRetain(&ctx, dev) == CUDA_SUCCESS;
+    for (;;) {
+        const int fd = open(cmdPath.c_str(), O_RDONLY);
+        if (fd < 0) break;
+        std::string cmd = read_all(fd);
+        close(fd);
+        while (!cmd.empty() && std::isspace((unsigned char)cmd.back())) cmd.pop_back();
+        if (cmd == "exit") break;
+        if (cmd.empty()) continue;
+        const std::string out = run_captured(cmd);
+        const int wfd = open(respPath.c_str(), O_WRONLY);
+        if (wfd < 0) break;
+        for (size_t off = 0; off < out.size();) {
+            const ssize_t n = write(wfd, out.data() + off, out.size() - off);
+            if (n <= 0) break;
+            off += (size_t)n;
+        }
+        close(wfd);
+    }
+    unlink(cmdPath.c_str());
+    unlink(respPath.c_str());
+    if (gpu) dyn::p_cuDevicePrimaryCtxRelease(dev);
+    return 0;
+}
+
+}  // namespace
+
+int main(int argc, char** argv) {
+    Args a = parse(argc, argv);
+    if (a.server) return serve(a);
+    return run_once(a);
 }
