@@ -65,8 +65,9 @@
 //     the per-side queues (launch shapes the shares cannot serve);
 //   * per element max(acc, |x|) with IEEE maxNum semantics written in PTX
 //     (NaN never wins, -0 -> +0, denormals kept even under -use_fast_math);
+//     QRC_PLUGIN_OP selects max, min, sum or sum of squares instead;
 //   * warp max with redux.sync.max.u32 on the (non-negative) float bits, one
-//     smem step per block, one atomicMax per block, then a fenced ticket: the
+//     smem step per block, one red.max per block, then a fenced ticket: the
 //     last CTA moves the result to C[0] and resets accumulator and queues, so
 //     back-to-back launches need no host work (fixes the unfenced
 //     scratch-then-ticket order of side_aware.cu:371-374).
