@@ -228,6 +228,26 @@ int qrc_xchg_set_peer(qrc_xchg* x, int peer, const void* handle);
 int qrc_xchg_destroy(qrc_xchg* x);
 int qrc_absmax_f32_allreduce(const float* d_in, size_t n, float* d_out, qrc_ctx* ctx, qrc_xchg* x, void* stream);
 
+/* Device memory homed like a context's buffer: *d_ptr points to ctx's buffer
+ * size of new memory at the same offset within its first 2 MiB page, built
+ * from physical 2 MiB pages chosen (by a discovery run over candidate pages)
+ * so that every offset lands on the same die as in the context's buffer.
+ * Element-wise work that reads x on its die can then write y there too.
+ * Allocates through the driver's virtual memory management (cuMemCreate /
+ * cuMemMap), temporarily about twice the buffer size.  Synchronous.  Free
+ * with qrc_free_like once no work uses the memory.
+ * Replaces: nothing in the reference; its README (README.md:14) notes that
+ * side-aware element-wise output needs this allocator-level page control. */
+typedef struct qrc_vmm_buf qrc_vmm_buf;
+int qrc_alloc_like(qrc_vmm_buf** out, void** d_ptr, const qrc_ctx* like);
+int qrc_free_like(qrc_vmm_buf* buf);
+
+/* d_y[i] = d_x[i] for n floats.  When d_x lies in ctx's buffer (16-byte
+ * aligned, d_y too, not overlapping) each die copies the chunks homed on it;
+ * with d_y from qrc_alloc_like the stores stay on the die as well.  Other
+ * cases use cudaMemcpyAsync.  Asynchronous.  No reference counterpart. */
+int qrc_copy_f32(const float* d_x, float* d_y, size_t n, qrc_ctx* ctx, void* stream);
+
 /* Synthetic inputs generated on the device; element i of the stream is a pure
  * function of (seed, offset + i), so shards of one stream can be generated
  * independently.  uniform[-1,1) on a 2^-23 grid; normal(0, sigma) is the

@@ -69,6 +69,9 @@ SIGNATURES = [
     ("qrc_ctx_set_overlap", c_int, [c_void_p, c_int]),
     ("qrc_absmax_f32", c_int, [c_void_p, c_size, c_void_p, c_void_p, c_void_p]),
     ("qrc_reduce_f32", c_int, [c_void_p, c_size, c_int, c_void_p, c_void_p, c_void_p]),
+    ("qrc_alloc_like", c_int, [ctypes.POINTER(c_void_p), ctypes.POINTER(c_void_p), c_void_p]),
+    ("qrc_free_like", c_int, [c_void_p]),
+    ("qrc_copy_f32", c_int, [c_void_p, c_void_p, c_size, c_void_p, c_void_p]),
     ("qrc_xchg_create", c_int, [ctypes.POINTER(c_void_p), c_int, c_int, c_int]),
     ("qrc_xchg_get_handle", c_int, [c_void_p, c_void_p]),
     ("qrc_xchg_set_peer", c_int, [c_void_p, c_int, c_void_p]),

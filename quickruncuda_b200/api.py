@@ -49,6 +49,21 @@ def _nbytes(x) -> int:
     raise TypeError("pass nbytes= with a raw pointer")
 
 
+class _LikeBuffer:
+    """Owner of a qrc_alloc_like buffer, exposed to torch through
+    __cuda_array_interface__; freed when the last tensor using it goes."""
+
+    def __init__(self, lib, buf, ptr, n, device):
+        self.lib, self.buf, self.n, self.device = lib, buf, n, device
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<f4", "data": (ptr, False), "version": 3,
+                                         "strides": None, "stream": None}
+
+    def __del__(self):
+        if getattr(self, "buf", None) is not None and self.buf.value:
+            self.lib.qrc_free_like(self.buf)
+            self.buf = None
+
+
 class SideAwareContext:
     """Side discovery for one device allocation plus the scratch its
     reductions use.  One reduction in flight per context at a time."""
@@ -176,6 +191,27 @@ class SideAwareContext:
                   self.lib.qrc_reduce_f32(_ptr(x) or None, n, code, _ptr(out), self.handle,
                                           _stream_handle(stream, self.device) or None))
         return out
+
+    def alloc_like(self):
+        """A float32 CUDA tensor of this context's buffer size whose 2 MiB
+        pages are homed like the buffer's (qrc_alloc_like): element i sits on
+        the same die as the buffer's element i.  The memory is released when
+        the tensor (and every view of it) is gone."""
+        import torch
+        buf, ptr = ctypes.c_void_p(), ctypes.c_void_p()
+        nat.check(self.lib, "qrc_alloc_like", self.lib.qrc_alloc_like(ctypes.byref(buf), ctypes.byref(ptr), self.handle))
+        holder = _LikeBuffer(self.lib, buf, ptr.value, self.nbytes // 4, self.device)
+        t = torch.as_tensor(holder, device=f"cuda:{self.device}")
+        return t
+
+    def copy(self, x, y, n: Optional[int] = None, stream=None):
+        """y[:n] = x[:n] (float32 CUDA tensors); side-aware when x lies in
+        this context's buffer.  Asynchronous."""
+        n = int(x.numel()) if n is None else n
+        nat.check(self.lib, "qrc_copy_f32",
+                  self.lib.qrc_copy_f32(_ptr(x) or None, _ptr(y) or None, n, self.handle,
+                                        _stream_handle(stream, self.device) or None))
+        return y
 
     def absmax_host(self, x, n: Optional[int] = None, stream=None) -> float:
         """Same from a host buffer (numpy array or CPU tensor); synchronous."""

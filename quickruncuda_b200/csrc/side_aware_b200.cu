@@ -182,6 +182,7 @@ enum : qrc_u32 {
     H_XCHG_ERR = 106,                              // a peer's value never arrived (sticky until cleared)
     H_QUANT_TICKET = 107,                          // side-aware quantize pass: CTAs done
     H_EPOCH = 108,                                 // share-mark tag of the last launch with shares
+    H_COPY_TICKET = 109,                           // side-aware copy: CTAs done
     O_BITLAT = 128,                                // 21 raw latencies of the mask probes
     O_SM_SIDE = 256,                               // per SM: 0 unknown, else 1 + side + 2 * index within side
     O_SM_LAT = 512,                                // per SM raw anchor latency (cycles)
