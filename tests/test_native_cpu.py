@@ -61,6 +61,9 @@ def test_invalid_arguments_rejected_without_gpu(lib):
     assert lib.qrc_ctx_set_mode(None, 0) == -1
     assert lib.qrc_reduce_f32(None, 16, 3, None, None, None) == -1
     assert lib.qrc_xchg_create(None, 0, 0, 1) == -1
+    assert lib.qrc_alloc_like(None, None, None) == -1
+    assert lib.qrc_copy_f32(None, None, 16, None, None) == -1
+    assert lib.qrc_free_like(None) == 0
     assert lib.qrc_absmax_f32_allreduce(None, 16, None, None, None, None) == -1
     assert lib.qrc_ctx_destroy(None) == 0
 
