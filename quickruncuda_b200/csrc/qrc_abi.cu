@@ -14,6 +14,9 @@
 #include <cuda_runtime.h>
 #include <cstring>
 #include <cstdlib>
+#include <map>
+#include <mutex>
+#include <utility>
 #include <vector>
 #include <omp.h>
 
@@ -399,20 +402,28 @@ static size_t launch_smem(const qrc_ctx* c) {
     return c->bulk_slots ? (size_t)(c->threads / 32) * c->bulk_slots * qrc::kSlotStride : 0;
 }
 
+// Raises a kernel's dynamic shared memory limit on the current device to at
+// least `smem` (launches above 48 KiB need it).  The attribute is per device,
+// so what was granted is remembered per (kernel, device); thread-safe.
+static cudaError_t grant_smem(const void* kernel, size_t smem) {
+    if (smem <= 48 * 1024) return cudaSuccess;
+    static std::mutex mu;
+    static std::map<std::pair<const void*, int>, size_t> granted;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    std::lock_guard<std::mutex> lock(mu);
+    size_t& g = granted[{kernel, dev}];
+    if (smem <= g) return cudaSuccess;
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e == cudaSuccess) g = smem;
+    return e;
+}
+
 template <int T>
 static cudaError_t allow_smem(size_t smem) {
-    static size_t granted_f32 = 0, granted_bf16 = 0;   // per process; device-independent attribute
-    if (smem > granted_f32) {
-        cudaError_t e = cudaFuncSetAttribute(qrc_k_absmax_f32<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return e;
-        granted_f32 = smem;
-    }
-    if (smem > granted_bf16) {
-        cudaError_t e = cudaFuncSetAttribute(qrc_k_amax_bf16<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return e;
-        granted_bf16 = smem;
-    }
-    return cudaSuccess;
+    cudaError_t e = grant_smem((const void*)qrc_k_absmax_f32<T>, smem);
+    return e != cudaSuccess ? e : grant_smem((const void*)qrc_k_amax_bf16<T>, smem);
 }
 
 // Launches `kernel` with programmatic stream serialization when the context
@@ -564,13 +575,8 @@ QRC_API int qrc_absmax_f32(const float* d_in, size_t n, float* d_out, qrc_ctx* c
 
 template <class Op, int T>
 static cudaError_t launch_reduce_t(qrc_ctx* c, const float* in, qrc_u64 n, void* out, size_t smem, cudaStream_t s) {
-    static size_t granted = 0;                      // per process, as allow_smem
-    if (smem > granted) {
-        cudaError_t e = cudaFuncSetAttribute(qrc_k_reduce_f32<Op, T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)smem);
-        if (e != cudaSuccess) return e;
-        granted = smem;
-    }
+    const cudaError_t e = grant_smem((const void*)qrc_k_reduce_f32<Op, T>, smem);
+    if (e != cudaSuccess) return e;
     return launch(c, qrc_k_reduce_f32<Op, T>, c->num_sms * c->blocks_per_sm, T, smem, s, in, n, c->d_map, out,
                   (qrc_u32)c->mode);
 }
@@ -711,18 +717,17 @@ QRC_API int qrc_absmax_f32_allreduce(const float* d_in, size_t n, float* d_out, 
     const int grid = c->num_sms * c->blocks_per_sm;
     const size_t smem = launch_smem(c);
     const qrc_u32 mode = (qrc_u32)c->mode;
-    static size_t granted[3] = {0, 0, 0};
     switch (c->threads) {
         case 1024:
-            if (smem > granted[0]) { QRC_CK(cudaFuncSetAttribute(qrc_k_absmax_f32_xchg<1024>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)); granted[0] = smem; }
+            QRC_CK(grant_smem((const void*)qrc_k_absmax_f32_xchg<1024>, smem));
             QRC_CK(launch(c, qrc_k_absmax_f32_xchg<1024>, grid, 1024, smem, s, d_in, (qrc_u64)n, c->d_map, d_out, mode, xa));
             break;
         case 512:
-            if (smem > granted[1]) { QRC_CK(cudaFuncSetAttribute(qrc_k_absmax_f32_xchg<512>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)); granted[1] = smem; }
+            QRC_CK(grant_smem((const void*)qrc_k_absmax_f32_xchg<512>, smem));
             QRC_CK(launch(c, qrc_k_absmax_f32_xchg<512>, grid, 512, smem, s, d_in, (qrc_u64)n, c->d_map, d_out, mode, xa));
             break;
         default:
-            if (smem > granted[2]) { QRC_CK(cudaFuncSetAttribute(qrc_k_absmax_f32_xchg<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)); granted[2] = smem; }
+            QRC_CK(grant_smem((const void*)qrc_k_absmax_f32_xchg<256>, smem));
             QRC_CK(launch(c, qrc_k_absmax_f32_xchg<256>, grid, 256, smem, s, d_in, (qrc_u64)n, c->d_map, d_out, mode, xa));
             break;
     }
