@@ -170,7 +170,7 @@ int qrc_reduce_f32(const float* d_in, size_t n, int op, void* d_out, qrc_ctx* ct
  * only the buffers it works on, a process held to a fixed memory budget, or
  * code that must avoid the implicit synchronisation cudaMalloc may cause.
  * Neither this call nor anything it calls allocates: no context is needed,
- * and its scratch (side map, work queues, ticket, accumulator; 20 KiB) is a
+ * and its scratch (side map, work queues, ticket, finish slots; 36 KiB) is a
  * fixed array that every GPU loading this library holds until exit.  Runs on
  * the current device, asynchronously on `stream`.
  *   - Limit: the input may span at most 32768 pages of 2 MiB (64 GiB, about
@@ -182,16 +182,31 @@ int qrc_reduce_f32(const float* d_in, size_t n, int op, void* d_out, qrc_ctx* ct
  *     repeated calls on the same buffer reuse the map.
  *   - Every call on a device shares the one array, so calls that overlap on
  *     the GPU (other streams, other host threads) race; serialise them.
+ *   - The array's address is looked up once per device; do not call this
+ *     entry point again after cudaDeviceReset in the same process.
  * Result and errors as qrc_absmax_f32.  No counterpart in the reference. */
 int qrc_absmax_f32_noalloc(const float* d_in, size_t n, float* d_out, void* stream);
 
 /* Same result from a host buffer: copies h_in to a device staging buffer owned
- * by the context (allocated and side-mapped on first use, regrown when n grows),
- * reduces it and copies the result to *h_out.  Synchronous.  Pinned host memory
- * gives full PCIe bandwidth.
+ * by the context in 64 MiB chunks on the context's own copy stream, reduces
+ * each chunk on `stream` as soon as it has landed (so the reductions hide
+ * under the copies), takes the maximum of the chunk results on the device and
+ * copies it to *h_out.  The copies start after the work queued on `stream`
+ * before the call.  Synchronous.  Pinned host memory gives full PCIe
+ * bandwidth.  The staging is set up by the first call that needs it (or by
+ * qrc_host_reserve) and kept by the context.
  * Replaces: the harness' fill-and-copy of A (QuickRunCUDA.cpp:432-457) followed
  * by a kernel launch and the C dump (:594-615). */
 int qrc_absmax_f32_host(const float* h_in, size_t n, float* h_out, qrc_ctx* ctx, void* stream);
+
+/* Sets up the staging of qrc_absmax_f32_host for inputs of up to n floats
+ * ahead of time: a device buffer of n floats with its own side map
+ * (discovery runs on it, synchronously), a copy stream, one event and one
+ * partial-result float per 64 MiB chunk.  A larger n replaces the staging; a
+ * smaller one keeps it.  On failure nothing is kept and the next call retries.
+ * Replaces: the harness' allocation of A before its first launch
+ * (QuickRunCUDA.cpp:360-362). */
+int qrc_host_reserve(qrc_ctx* ctx, size_t n);
 
 /* Fused per-tensor FP8 quantize of n bf16 values (raw bit patterns):
  *   amax = max |x| (maxNum), *d_scale = 448 / amax (IEEE division; 1 when amax
@@ -234,8 +249,11 @@ int qrc_absmax_f32_allreduce(const float* d_in, size_t n, float* d_out, qrc_ctx*
  * so that every offset lands on the same die as in the context's buffer.
  * Element-wise work that reads x on its die can then write y there too.
  * Allocates through the driver's virtual memory management (cuMemCreate /
- * cuMemMap), temporarily about twice the buffer size.  Synchronous.  Free
- * with qrc_free_like once no work uses the memory.
+ * cuMemMap).  Candidate pages are created and classified in rounds; while
+ * it runs it holds, besides the pages it keeps (the buffer size), one round's
+ * candidates: twice the pages still missing plus 4, at most 8192 pages
+ * (16 GiB).  Synchronous.
+ * Free with qrc_free_like once no work uses the memory.
  * Replaces: nothing in the reference; its README (README.md:14) notes that
  * side-aware element-wise output needs this allocator-level page control. */
 typedef struct qrc_vmm_buf qrc_vmm_buf;
@@ -243,9 +261,10 @@ int qrc_alloc_like(qrc_vmm_buf** out, void** d_ptr, const qrc_ctx* like);
 int qrc_free_like(qrc_vmm_buf* buf);
 
 /* d_y[i] = d_x[i] for n floats.  When d_x lies in ctx's buffer (16-byte
- * aligned, d_y too, not overlapping) each die copies the chunks homed on it;
- * with d_y from qrc_alloc_like the stores stay on the die as well.  Other
- * cases use cudaMemcpyAsync.  Asynchronous.  No reference counterpart. */
+ * aligned, d_y too) each die copies the chunks homed on it; with d_y from
+ * qrc_alloc_like the stores stay on the die as well.  Other cases use
+ * cudaMemcpyAsync.  Ranges that partly overlap return QRC_ERR_INVALID;
+ * d_x == d_y does nothing.  Asynchronous.  No reference counterpart. */
 int qrc_copy_f32(const float* d_x, float* d_y, size_t n, qrc_ctx* ctx, void* stream);
 
 /* Synthetic inputs generated on the device; element i of the stream is a pure

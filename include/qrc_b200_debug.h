@@ -34,6 +34,15 @@ int qrc_is_checked_build(void);
  * an encoder written from the OCP OFP8 specification).  Asynchronous. */
 int qrc_debug_cvt_e4m3(const float* d_in, size_t n, uint8_t* d_out, void* stream);
 
+/* Plain streaming read of bytes [d_in, d_in + bytes) (16-byte aligned; a tail
+ * below 16 bytes is skipped) with no side logic, XOR-folded into *d_sink: a
+ * measured read-only ceiling for the roofline.  `depth` 16-byte loads in
+ * flight per thread; the shapes offered are (depth, threads, blocks per SM) =
+ * (8, 1024, 1), (4, 1024, 2), (16, 512, 1) and (32, 256, 1), all 128 KiB in
+ * flight per SM.  Runs on the current device.  Asynchronous. */
+int qrc_debug_read_stream(const void* d_in, size_t bytes, int depth, int threads, int blocks_per_sm,
+                          uint32_t* d_sink, void* stream);
+
 /* Device pointer of the context's side map (for launching the plugin kernels
  * from a test on the same scratch). */
 void* qrc_ctx_map_device_ptr(const struct qrc_ctx* ctx);
@@ -42,6 +51,17 @@ void* qrc_ctx_map_device_ptr(const struct qrc_ctx* ctx);
  * inside the context's mapped buffer and aligned; 0: always the side-agnostic
  * pass (for comparing the two). */
 int qrc_ctx_debug_quant_side_aware(struct qrc_ctx* ctx, int enable);
+
+/* 1 (default): qrc_amax_quant_e4m3 runs the single-launch fused kernel
+ * whenever its conditions hold (input inside the context's side-aware
+ * buffer, 16-byte aligned input, 8-byte aligned output, every SM labelled by
+ * discovery, a cooperative launch of one CTA per SM fits); 0: always the two
+ * launches (amax pass, then quantize pass), for comparing the two. */
+int qrc_ctx_debug_quant_fused(struct qrc_ctx* ctx, int enable);
+
+/* Kernel launches qrc_amax_quant_e4m3 would make for these arguments: 1 (the
+ * fused kernel, or n == 0) or 2. */
+int qrc_debug_quant_launches(struct qrc_ctx* ctx, const uint16_t* d_in, size_t n, const uint8_t* d_q);
 
 /* Exchange tests on one GPU: map a peer's slot array to a local device buffer
  * (no IPC), read this rank's slot array, and the epoch of the last launch.

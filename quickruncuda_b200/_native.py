@@ -80,10 +80,13 @@ SIGNATURES = [
     ("qrc_xchg_debug_set_peer_ptr", c_int, [c_void_p, c_int, c_void_p]),
     ("qrc_xchg_debug_slots", c_void_p, [c_void_p]),
     ("qrc_ctx_debug_quant_side_aware", c_int, [c_void_p, c_int]),
+    ("qrc_ctx_debug_quant_fused", c_int, [c_void_p, c_int]),
+    ("qrc_debug_quant_launches", c_int, [c_void_p, c_void_p, c_size, c_void_p]),
     ("qrc_xchg_debug_post", c_int, [c_void_p, c_int, ctypes.c_uint32, ctypes.c_uint32]),
     ("qrc_xchg_epoch", ctypes.c_uint32, [c_void_p]),
     ("qrc_absmax_f32_noalloc", c_int, [c_void_p, c_size, c_void_p, c_void_p]),
     ("qrc_absmax_f32_host", c_int, [c_void_p, c_size, ctypes.POINTER(c_float), c_void_p, c_void_p]),
+    ("qrc_host_reserve", c_int, [c_void_p, c_size]),
     ("qrc_amax_quant_e4m3", c_int, [c_void_p, c_size, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
     ("qrc_fill_uniform_f32", c_int, [c_void_p, c_size, c_u64, c_u64, c_void_p]),
     ("qrc_fill_normal_f32", c_int, [c_void_p, c_size, c_u64, c_u64, c_float, c_void_p]),
@@ -102,6 +105,7 @@ SIGNATURES = [
     ("qrc_is_checked_build", c_int, []),
     ("qrc_ctx_map_device_ptr", c_void_p, [c_void_p]),
     ("qrc_debug_cvt_e4m3", c_int, [c_void_p, c_size, c_void_p, c_void_p]),
+    ("qrc_debug_read_stream", c_int, [c_void_p, c_size, c_int, c_int, c_int, c_void_p, c_void_p]),
 ]
 
 

@@ -241,6 +241,19 @@ class SideAwareContext:
                                                _stream_handle(stream, self.device) or None))
         return q, scale, amax
 
+    def quant_launches(self, x_bf16, q=None) -> int:
+        """Kernel launches amax_quant_e4m3 makes for this input and output:
+        1 (the single-launch fused kernel) or 2 (amax pass, quantize pass)."""
+        r = self.lib.qrc_debug_quant_launches(self.handle, _ptr(x_bf16) or None, int(x_bf16.numel()),
+                                              _ptr(q) or None)
+        if r < 0:
+            nat.check(self.lib, "qrc_debug_quant_launches", r)
+        return int(r)
+
+    def set_quant_fused(self, enable: bool) -> None:
+        """Allow (default) or forbid the single-launch fused quantize."""
+        nat.check(self.lib, "qrc_ctx_debug_quant_fused", self.lib.qrc_ctx_debug_quant_fused(self.handle, int(bool(enable))))
+
     # -- diagnostics -------------------------------------------------------
     def read_map(self, words: Optional[int] = None) -> np.ndarray:
         total = ctypes.c_size_t()

@@ -216,6 +216,240 @@ qrc_k_quant_e4m3_sa(const uint16_t* in, qrc_u64 n, uint8_t* q, const float* scal
     }
 }
 
+// ---- single-launch fused amax -> e4m3 --------------------------------------
+//
+// One cooperative launch, one 1024-thread CTA per SM.  Every CTA walks its
+// static side-local share (the share layout of read_share: the CTA on SM
+// (s, k) owns the 64 KiB blocks b = k*4 + g + i*4*K_s, its group g reads the
+// side-s 4 KiB chunk of each of the block's 8 pairs, 128 B per thread per
+// block).  Phase 1 takes the amax and keeps the last kFusedStash blocks each
+// thread read on the chip: two in tensor memory (tcgen05.st into the
+// thread's TMEM lane, 64 columns per warp, all 512 columns per CTA) and one
+// in shared memory (128 KiB per CTA).  A bounded grid barrier hands the
+// global amax to every CTA.  Phase 2 quantizes the stash first (no HBM
+// read), then the rest of the share in reverse order, so the blocks read
+// last in phase 1, the ones most likely still in L2, are read first.  About
+// 58 MB of a 268 MB input never cross HBM twice.
+// Edges outside the 64 KiB-aligned body are read by CTA 0 element by
+// element in both phases.  The last CTA to finish (ticket) publishes amax and
+// scale and resets the barrier words for the next launch.  If the barrier
+// wait gives up (about 1 s) or a share was not read, amax and scale are NaN
+// and H_FUSED_ERR is set; TMEM is freed on every path.
+constexpr int kFusedTmemIters = 2;
+constexpr int kFusedSmemIters = 1;
+constexpr int kFusedStash = kFusedTmemIters + kFusedSmemIters;
+constexpr qrc_u32 kFusedSmemBytes = 1024u * 128u * kFusedSmemIters;
+constexpr long long kFusedWaitCycles = 1ll << 31;          // about one second
+// Phase 1 reads the kFusedL2Iters blocks before the stash with the default
+// L2 policy and every other block evict-first, so what phase 2 reads first
+// from memory (those blocks) is what L2 keeps: 5 x 148 x 128 KiB = 97 MB.
+#ifndef QRC_FUSED_L2_ITERS
+#define QRC_FUSED_L2_ITERS 5
+#endif
+constexpr int kFusedL2Iters = QRC_FUSED_L2_ITERS;
+
+static __device__ __forceinline__ void tmem_st_x32(qrc_u32 taddr, const uint4 (&v)[8]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+                 "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+                 "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};\n\t"
+                 "tcgen05.wait::st.sync.aligned;"
+                 :: "r"(taddr),
+                    "r"(v[0].x), "r"(v[0].y), "r"(v[0].z), "r"(v[0].w), "r"(v[1].x), "r"(v[1].y), "r"(v[1].z), "r"(v[1].w),
+                    "r"(v[2].x), "r"(v[2].y), "r"(v[2].z), "r"(v[2].w), "r"(v[3].x), "r"(v[3].y), "r"(v[3].z), "r"(v[3].w),
+                    "r"(v[4].x), "r"(v[4].y), "r"(v[4].z), "r"(v[4].w), "r"(v[5].x), "r"(v[5].y), "r"(v[5].z), "r"(v[5].w),
+                    "r"(v[6].x), "r"(v[6].y), "r"(v[6].z), "r"(v[6].w), "r"(v[7].x), "r"(v[7].y), "r"(v[7].z), "r"(v[7].w)
+                 : "memory");
+}
+static __device__ __forceinline__ void tmem_ld_x32(qrc_u32 taddr, uint4 (&v)[8]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+                 "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+                 "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];\n\t"
+                 "tcgen05.wait::ld.sync.aligned;"
+                 : "=r"(v[0].x), "=r"(v[0].y), "=r"(v[0].z), "=r"(v[0].w), "=r"(v[1].x), "=r"(v[1].y), "=r"(v[1].z), "=r"(v[1].w),
+                   "=r"(v[2].x), "=r"(v[2].y), "=r"(v[2].z), "=r"(v[2].w), "=r"(v[3].x), "=r"(v[3].y), "=r"(v[3].z), "=r"(v[3].w),
+                   "=r"(v[4].x), "=r"(v[4].y), "=r"(v[4].z), "=r"(v[4].w), "=r"(v[5].x), "=r"(v[5].y), "=r"(v[5].z), "=r"(v[5].w),
+                   "=r"(v[6].x), "=r"(v[6].y), "=r"(v[6].z), "=r"(v[6].w), "=r"(v[7].x), "=r"(v[7].y), "=r"(v[7].z), "=r"(v[7].w)
+                 : "r"(taddr) : "memory");
+}
+
+// Address of chunk j (0..7) of 64 KiB block `base` for thread t of a group of
+// side s: the pair's half homed on s (see ChunkMap::chunk_of).
+static __device__ __forceinline__ qrc_u32 fused_second(const qrc::ChunkMap& cm, qrc_u64 base, int s, qrc_u32 pat) {
+    int pbit = 0;
+    if (cm.use_page_bits) {
+        const qrc_u64 pg = (base - cm.page_base) >> 21;
+        pbit = (int)(cm.page_bits[pg >> 5] >> (pg & 31)) & 1;
+    }
+    return (qrc_u32)(qrc::parity64(base & cm.mask) ^ pbit ^ cm.flip ^ s) ? ~pat : pat;
+}
+
+static __device__ __forceinline__ uint8_t quant_one(uint16_t x, float s) {
+    return (uint8_t)(cvt_e4m3x2(0.0f, __fmul_rn(__uint_as_float((qrc_u32)x << 16), s)) & 0xFFu);
+}
+
+__global__ void __launch_bounds__(1024, 1)
+qrc_k_amax_quant_fused(const uint16_t* in, qrc_u64 n, uint8_t* q, float* amax_out, float* scale_out, qrc_u32* map,
+                       qrc_u32 mode) {
+    using namespace qrc;
+    extern __shared__ __align__(128) uint4 s_stash[];          // kFusedSmemIters x 8 x 1024 uint4
+    __shared__ qrc_u32 s_taddr;
+    __shared__ float s_scale;
+    __shared__ int s_ok, s_last;
+    const int tid = threadIdx.x, warp = tid >> 5, g = tid >> 8, t = tid & 255;
+    const qrc_u64 a = (qrc_u64)in, end = a + 2 * n;
+    ChunkMap cm;
+    cm.setup(a, end, map, mode & ~SCHED_MASK);                 // header only: written by discovery alone
+    const qrc_u32 k0 = map[H_NSIDE0], k1 = map[H_NSIDE1];
+    const int s = cm.side, k = cm.sm_index;
+    const qrc_u32 Ks = s ? k1 : k0;
+    const bool has_share = cm.aware && k >= 0 && (qrc_u32)k < Ks && Ks <= 128u;
+    const qrc_u64 lo64 = (a + 0xFFFFull) & ~0xFFFFull;
+    const qrc_u64 nbf = end > lo64 ? (end - lo64) >> 16 : 0;   // whole 64 KiB blocks of the body
+    const qrc_u64 body_end = lo64 + (nbf << 16);
+    const qrc_u64 stride = (qrc_u64)Ks * 4u, b0 = (qrc_u64)k * 4u + (qrc_u64)g;
+    const qrc_u64 m = (has_share && b0 < nbf) ? (nbf - b0 + stride - 1) / stride : 0;
+    qrc_u32 pat = 0;
+    #pragma unroll
+    for (int j = 0; j < 8; j++) pat |= (qrc_u32)parity64(((qrc_u64)j << 13) & cm.mask) << j;
+
+    // Tensor memory: all 512 columns; warp w owns lanes (w % 4) * 32 .. + 31
+    // of columns (w / 4) * 64 .. + 63, i.e. two 32-column slots per thread.
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;"
+                     :: "r"((qrc_u32)__cvta_generic_to_shared(&s_taddr)) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const qrc_u32 tslot = s_taddr + ((qrc_u32)((warp & 3) * 32) << 16) + (qrc_u32)(warp >> 2) * 64u;
+    griddep_wait();
+
+    // ---- phase 1: amax, keeping the last blocks on the chip ------------------
+    qrc_u32 acc = 0;                                           // two bf16 lanes of max |x|
+    for (qrc_u64 i = 0; i < m; i++) {
+        const qrc_u64 base = lo64 + ((b0 + i * stride) << 16);
+        const qrc_u32 second = fused_second(cm, base, s, pat);
+        const qrc_u64 row = base + 16ull * t;
+        const qrc_u64 r = m - 1 - i;
+        const bool keep_in_l2 = r >= (qrc_u64)kFusedStash && r < (qrc_u64)(kFusedStash + kFusedL2Iters);
+        uint4 v[8];
+        if (keep_in_l2) {
+            #pragma unroll
+            for (int j = 0; j < 8; j++)
+                v[j] = ld16<1>(row + ((qrc_u64)j << 13) + ((qrc_u64)((second >> j) & 1u) << 12));
+        } else {
+            #pragma unroll
+            for (int j = 0; j < 8; j++)
+                v[j] = ld16<2>(row + ((qrc_u64)j << 13) + ((qrc_u64)((second >> j) & 1u) << 12));
+        }
+        #pragma unroll
+        for (int j = 0; j < 8; j++) acc = OpAbsBF16::step16(acc, v[j]);
+        if (r < (qrc_u64)kFusedTmemIters) {
+            tmem_st_x32(tslot + 32u * (qrc_u32)r, v);
+        } else if (r < (qrc_u64)kFusedStash) {
+            uint4* sp = s_stash + (size_t)(r - kFusedTmemIters) * 8192 + tid;
+            #pragma unroll
+            for (int j = 0; j < 8; j++) sp[j * 1024] = v[j];
+        }
+    }
+    // Edges, element by element: [a, lo64) and [body_end, end), both empty or
+    // shorter than 64 KiB (when end <= lo64 the head is the whole input).
+    const qrc_u64 head_n = ((lo64 < end ? lo64 : end) - a) >> 1, tail_e = (body_end - a) >> 1;
+    if (blockIdx.x == 0) {
+        for (qrc_u64 e = tid; e < head_n; e += blockDim.x) acc = absmax_step_bf16x2(acc, (qrc_u32)in[e]);
+        for (qrc_u64 e = tail_e + tid; e < n; e += blockDim.x) acc = absmax_step_bf16x2(acc, (qrc_u32)in[e]);
+    }
+
+    // ---- grid barrier: the amax of every CTA, and which shares were read -----
+    const qrc_u32 v = block_max(OpAbsBF16::to_red(acc));
+    if (tid == 0) {
+        asm volatile("red.relaxed.gpu.global.max.u32 [%0], %1;" :: "l"(&map[H_FUSED_ACC]), "r"(v) : "memory");
+        if (has_share) atomicOr(&map[O_FUSED_SHARES + ((qrc_u32)s * 128u + (qrc_u32)k) / 32u], 1u << (k & 31));
+        qrc_u32 arrived;
+        asm volatile("atom.release.gpu.global.add.u32 %0, [%1], 1;" : "=r"(arrived) : "l"(&map[H_FUSED_ARRIVE]) : "memory");
+        bool ok = true;
+        const long long t0 = clock64();
+        for (;;) {
+            asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(arrived) : "l"(&map[H_FUSED_ARRIVE]) : "memory");
+            if (arrived >= gridDim.x) break;
+            if (clock64() - t0 > kFusedWaitCycles) { ok = false; break; }
+            __nanosleep(100);
+        }
+        float amax = __int_as_float(0x7FFFFFFF);
+        if (ok) {
+            amax = __uint_as_float(__ldcg(&map[H_FUSED_ACC]));
+            for (int w = 0; w < 8; w++) {                       // every share of both sides was read
+                const qrc_u32 K = (w >> 2) ? k1 : k0, lo = (qrc_u32)(w & 3) * 32u;
+                const qrc_u32 req = K <= lo ? 0u : (K - lo >= 32u ? 0xFFFFFFFFu : (1u << (K - lo)) - 1u);
+                if ((__ldcg(&map[O_FUSED_SHARES + w]) & req) != req) ok = false;
+            }
+        }
+        if (!ok) atomicExch(&map[H_FUSED_ERR], 1u);
+        s_ok = ok;
+        s_scale = e4m3_scale_from_amax(amax);
+    }
+    __syncthreads();
+
+    // ---- phase 2: quantize, the stash first, then the share backwards ---------
+    if (s_ok) {
+        const float sc = s_scale;
+        for (qrc_u64 r = 0; r < m; r++) {
+            const qrc_u64 base = lo64 + ((b0 + (m - 1 - r) * stride) << 16);
+            const qrc_u32 second = fused_second(cm, base, s, pat);
+            const qrc_u64 row = base + 16ull * t;
+            uint4 v[8];
+            if (r < (qrc_u64)kFusedTmemIters) {
+                tmem_ld_x32(tslot + 32u * (qrc_u32)r, v);
+            } else if (r < (qrc_u64)kFusedStash) {
+                const uint4* sp = s_stash + (size_t)(r - kFusedTmemIters) * 8192 + tid;
+                #pragma unroll
+                for (int j = 0; j < 8; j++) v[j] = sp[j * 1024];
+            } else {
+                #pragma unroll
+                for (int j = 0; j < 8; j++)
+                    v[j] = ld16<2>(row + ((qrc_u64)j << 13) + ((qrc_u64)((second >> j) & 1u) << 12));
+            }
+            #pragma unroll
+            for (int j = 0; j < 8; j++) {
+                const qrc_u64 x = row + ((qrc_u64)j << 13) + ((qrc_u64)((second >> j) & 1u) << 12);
+                quant16(v[j], sc, q + ((x - a) >> 1));
+            }
+        }
+        if (blockIdx.x == 0) {
+            for (qrc_u64 e = tid; e < head_n; e += blockDim.x) q[e] = quant_one(in[e], sc);
+            for (qrc_u64 e = tail_e + tid; e < n; e += blockDim.x) q[e] = quant_one(in[e], sc);
+        }
+    }
+
+    // ---- tensor memory back, then the last CTA publishes and resets -----------
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 0) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" :: "r"(s_taddr) : "memory");
+    }
+    griddep_launch_dependents();
+    if (tid == 0) {
+        qrc_u32 tk;
+        asm volatile("atom.acq_rel.gpu.global.inc.u32 %0, [%1], %2;"
+                     : "=r"(tk) : "l"(&map[H_FUSED_DONE]), "r"(gridDim.x - 1) : "memory");
+        s_last = tk == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (s_last && tid == 0) {
+        const bool err = __ldcg(&map[H_FUSED_ERR]) != 0u;
+        const float amax = err ? __int_as_float(0x7FFFFFFF) : __uint_as_float(__ldcg(&map[H_FUSED_ACC]));
+        *amax_out = amax;
+        *scale_out = e4m3_scale_from_amax(amax);              // 1 for a NaN amax, as in the two-pass path
+        if (err) map[H_WAIT_ERR] |= 2u;                        // sticky record for diagnostics
+        map[H_FUSED_ERR] = 0u;
+        map[H_FUSED_ACC] = 0u;
+        map[H_FUSED_ARRIVE] = 0u;
+        for (int w = 0; w < 8; w++) map[O_FUSED_SHARES + w] = 0u;
+    }
+}
+
 // Side-aware copy y = x: the same group claims as qrc_k_quant_e4m3_sa, each
 // group copying the 4 KiB chunk of every pair that is homed on its die.  With
 // y from qrc_alloc_like (same offset in its 2 MiB page, pages homed like
@@ -304,6 +538,31 @@ qrc_k_copy_f32_sa(const float* x, qrc_u64 n, float* y, qrc_u32* map, qrc_u32 mod
     }
 }
 
+// Plain streaming read of [p, p + bytes) with no side logic: a grid-stride
+// walk over 16-byte units, D loads in flight per thread, folded by XOR into
+// one word per warp (so the loads cannot be dropped).  A measuring stick for
+// what a read-only stream reaches on this GPU; the tail (bytes % 16) is left
+// out.
+template <int D, int T, int B>
+__global__ void __launch_bounds__(T, B)
+qrc_k_read_stream(const uint4* p, qrc_u64 nv, qrc_u32* sink) {
+    const qrc_u64 tid = (qrc_u64)blockIdx.x * blockDim.x + threadIdx.x;
+    const qrc_u64 stride = (qrc_u64)gridDim.x * blockDim.x;
+    qrc_u32 x = 0;
+    for (qrc_u64 i = tid; i < nv; i += D * stride) {
+        uint4 v[D];
+        #pragma unroll
+        for (int u = 0; u < D; u++) {
+            const qrc_u64 j = i + u * stride;
+            v[u] = j < nv ? qrc::ld_stream16((qrc_u64)(p + j)) : make_uint4(0, 0, 0, 0);
+        }
+        #pragma unroll
+        for (int u = 0; u < D; u++) x ^= v[u].x ^ v[u].y ^ v[u].z ^ v[u].w;
+    }
+    x = __reduce_xor_sync(0xFFFFFFFFu, x);
+    if ((threadIdx.x & 31) == 0) atomicXor(sink, x);
+}
+
 __global__ void qrc_k_debug_cvt_e4m3(const float* in, qrc_u64 n, uint8_t* out) {
     for (qrc_u64 i = (qrc_u64)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (qrc_u64)gridDim.x * blockDim.x)
         out[i] = (uint8_t)(cvt_e4m3x2(0.0f, in[i]) & 0xFFu);
@@ -367,15 +626,23 @@ struct qrc_ctx {
     int bulk_slots = 0;             // 0: register loads; >= 2: bulk-copy staging slots per warp
     int overlap = 1;                // programmatic dependent launch of reductions
     int quant_side_aware = 1;       // side-aware quantize pass when the input is mapped
+    int quant_fused = 1;            // single-launch fused quantize when its conditions hold
+    int fused_checked = 0;          // 0 not yet, 1 the fused launch fits this device, -1 it does not
     const void* base = nullptr;
     size_t bytes = 0;
     qrc_u32* d_map = nullptr;
     size_t map_words = 0;
     qrc_side_info info{};
     float* d_scalars = nullptr;     // [0] amax scratch, [1] host-path result
-    float* d_stage = nullptr;       // host-buffer staging (qrc_absmax_f32_host)
-    size_t stage_cap = 0;           // floats
-    qrc_ctx* stage_ctx = nullptr;   // side map of the staging buffer
+    // host-buffer path (qrc_absmax_f32_host): staging buffer with its own side
+    // map, a copy stream, one event and one partial result per chunk
+    float* d_stage = nullptr;
+    size_t stage_cap = 0;           // floats; 0 until qrc_host_reserve succeeded
+    qrc_ctx* stage_ctx = nullptr;
+    cudaStream_t copy_stream = nullptr;
+    cudaEvent_t entry_event = nullptr;
+    std::vector<cudaEvent_t> chunk_events;
+    float* d_partials = nullptr;    // one float per chunk
 };
 
 static void fill_info(qrc_ctx* c, const qrc_u32* h) {
@@ -509,11 +776,23 @@ QRC_API int qrc_ctx_create(qrc_ctx** out, int device, const void* d_base, size_t
     return QRC_OK;
 }
 
+// Frees the host-buffer path's staging (buffer, its context, stream, events,
+// partials) and marks it absent.
+static void host_release(qrc_ctx* c) {
+    if (c->stage_ctx) { qrc_ctx_destroy(c->stage_ctx); c->stage_ctx = nullptr; }
+    if (c->d_stage) { cudaFree(c->d_stage); c->d_stage = nullptr; }
+    if (c->d_partials) { cudaFree(c->d_partials); c->d_partials = nullptr; }
+    for (cudaEvent_t e : c->chunk_events) cudaEventDestroy(e);
+    c->chunk_events.clear();
+    if (c->entry_event) { cudaEventDestroy(c->entry_event); c->entry_event = nullptr; }
+    if (c->copy_stream) { cudaStreamDestroy(c->copy_stream); c->copy_stream = nullptr; }
+    c->stage_cap = 0;
+}
+
 QRC_API int qrc_ctx_destroy(qrc_ctx* c) {
     if (!c) return QRC_OK;
     DeviceScope scope(c->device);
-    if (c->stage_ctx) qrc_ctx_destroy(c->stage_ctx);
-    if (c->d_stage) cudaFree(c->d_stage);
+    host_release(c);
     if (c->d_map) cudaFree(c->d_map);
     if (c->d_scalars) cudaFree(c->d_scalars);
     delete c;
@@ -734,31 +1013,123 @@ QRC_API int qrc_absmax_f32_allreduce(const float* d_in, size_t n, float* d_out, 
     return QRC_OK;
 }
 
+// Host-buffer path: the input crosses PCIe in chunks of kHostChunkFloats on a
+// copy stream, and each chunk is reduced on the caller's stream as soon as it
+// has landed, so the reduction hides under the copy of the next chunk; one
+// small kernel then takes the maximum of the per-chunk results.
+constexpr size_t kHostChunkFloats = 16ull << 20;          // 64 MiB: 32 whole 2 MiB pages
+
+// Maximum of `k` per-chunk results.  An unsigned maximum of the bit patterns:
+// the results are non-negative floats or NaN (a reduction whose bounded wait
+// gave up), and the NaN pattern 0x7FFFFFFF orders above every one of them.
+__global__ void qrc_k_max_partials(const float* partials, qrc_u32 k, float* out) {
+    qrc_u32 m = 0;
+    for (qrc_u32 i = threadIdx.x; i < k; i += blockDim.x) {
+        const qrc_u32 b = __float_as_uint(partials[i]);
+        m = b > m ? b : m;
+    }
+    m = qrc::block_max(m);
+    if (threadIdx.x == 0) *out = __uint_as_float(m);
+}
+
+QRC_API int qrc_host_reserve(qrc_ctx* c, size_t n) {
+    if (!c) return QRC_ERR_INVALID;
+    if (n > ((size_t)1 << 61)) return QRC_ERR_RANGE;
+    if (n <= c->stage_cap) return QRC_OK;
+    DeviceScope scope(c->device);
+    if (!scope.ok) return QRC_ERR_STATE;
+    host_release(c);                                       // capacity stays 0 until all of it exists
+    const size_t chunks = (n + kHostChunkFloats - 1) / kHostChunkFloats;
+    int rc = QRC_OK;
+    do {
+        if (cudaMalloc(&c->d_stage, n * sizeof(float)) != cudaSuccess ||
+            cudaMalloc(&c->d_partials, chunks * sizeof(float)) != cudaSuccess ||
+            cudaStreamCreateWithFlags(&c->copy_stream, cudaStreamNonBlocking) != cudaSuccess ||
+            cudaEventCreateWithFlags(&c->entry_event, cudaEventDisableTiming) != cudaSuccess) {
+            rc = QRC_ERR_CUDA; break;
+        }
+        c->chunk_events.reserve(chunks);
+        for (size_t i = 0; i < chunks && rc == QRC_OK; i++) {
+            cudaEvent_t e;
+            if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) rc = QRC_ERR_CUDA;
+            else c->chunk_events.push_back(e);
+        }
+        if (rc != QRC_OK) break;
+        rc = qrc_ctx_create(&c->stage_ctx, c->device, c->d_stage, n * sizeof(float), nullptr);
+    } while (0);
+    if (rc != QRC_OK) {
+        if (rc == QRC_ERR_CUDA && g_last_cuda == 0) g_last_cuda = (int)cudaGetLastError();
+        host_release(c);
+        return rc;
+    }
+    c->stage_ctx->mode = c->mode;
+    c->stage_ctx->blocks_per_sm = c->blocks_per_sm;
+    c->stage_ctx->threads = c->threads;
+    c->stage_ctx->bulk_slots = c->bulk_slots;
+    c->stage_ctx->overlap = c->overlap;
+    c->stage_cap = n;
+    return QRC_OK;
+}
+
 QRC_API int qrc_absmax_f32_host(const float* h_in, size_t n, float* h_out, qrc_ctx* c, void* stream) {
     if (!c || !h_out || (n && !h_in)) return QRC_ERR_INVALID;
+    if (n > ((size_t)1 << 61)) return QRC_ERR_RANGE;
     DeviceScope scope(c->device);
     if (!scope.ok) return QRC_ERR_STATE;
     cudaStream_t s = as_stream(stream);
-    if (n > c->stage_cap) {
-        if (c->stage_ctx) { qrc_ctx_destroy(c->stage_ctx); c->stage_ctx = nullptr; }
-        if (c->d_stage) { cudaFree(c->d_stage); c->d_stage = nullptr; c->stage_cap = 0; }
-        QRC_CK(cudaMalloc(&c->d_stage, n * sizeof(float)));
-        c->stage_cap = n;
-        const int rc = qrc_ctx_create(&c->stage_ctx, c->device, c->d_stage, n * sizeof(float), stream);
-        if (rc != QRC_OK) return rc;
-        c->stage_ctx->mode = c->mode;
-        c->stage_ctx->blocks_per_sm = c->blocks_per_sm;
-        c->stage_ctx->threads = c->threads;
-        c->stage_ctx->bulk_slots = c->bulk_slots;
-        c->stage_ctx->overlap = c->overlap;
+    if (n == 0) { *h_out = 0.0f; return QRC_OK; }
+    const int rr = qrc_host_reserve(c, n);
+    if (rr != QRC_OK) return rr;
+    qrc_ctx* sc = c->stage_ctx;
+    const size_t chunks = (n + kHostChunkFloats - 1) / kHostChunkFloats;
+    // The copies start after everything the caller queued on `stream` before
+    // this call (which may still be producing h_in, or reading the staging).
+    QRC_CK(cudaEventRecord(c->entry_event, s));
+    QRC_CK(cudaStreamWaitEvent(c->copy_stream, c->entry_event, 0));
+    for (size_t i = 0; i < chunks; i++) {
+        const size_t off = i * kHostChunkFloats, len = n - off < kHostChunkFloats ? n - off : kHostChunkFloats;
+        QRC_CK(cudaMemcpyAsync(c->d_stage + off, h_in + off, len * sizeof(float), cudaMemcpyHostToDevice,
+                               c->copy_stream));
+        QRC_CK(cudaEventRecord(c->chunk_events[i], c->copy_stream));
     }
-    qrc_ctx* sc = c->stage_ctx ? c->stage_ctx : c;
-    if (n) QRC_CK(cudaMemcpyAsync(c->d_stage, h_in, n * sizeof(float), cudaMemcpyHostToDevice, s));
-    const int rc = launch_absmax(sc, c->d_stage, n, c->d_scalars + 1, s);
-    if (rc != QRC_OK) return rc;
+    for (size_t i = 0; i < chunks; i++) {
+        const size_t off = i * kHostChunkFloats, len = n - off < kHostChunkFloats ? n - off : kHostChunkFloats;
+        QRC_CK(cudaStreamWaitEvent(s, c->chunk_events[i], 0));
+        const int rc = launch_absmax(sc, c->d_stage + off, len, c->d_partials + i, s);
+        if (rc != QRC_OK) return rc;
+    }
+    qrc_k_max_partials<<<1, 256, 0, s>>>(c->d_partials, (qrc_u32)chunks, c->d_scalars + 1);
+    QRC_CK(cudaGetLastError());
     QRC_CK(cudaMemcpyAsync(h_out, c->d_scalars + 1, sizeof(float), cudaMemcpyDeviceToHost, s));
     QRC_CK(cudaStreamSynchronize(s));
     return QRC_OK;
+}
+
+// Whether the single-launch fused quantize can run: the input inside the
+// context's side-aware buffer, vector-aligned, every SM labelled by discovery
+// (each SM gets exactly one CTA of a cooperative launch, so every static
+// share is read once), and a cooperative launch of one 1024-thread CTA per
+// SM with the stash's shared memory fits.
+static bool fused_quant_ok(qrc_ctx* c, const uint16_t* d_in, size_t n, const uint8_t* d_q) {
+    if (!c->quant_fused || !n) return false;
+    const bool mapped = c->info.status == QRC_SIDE_OK && (uintptr_t)d_in >= (uintptr_t)c->base &&
+                        (uintptr_t)d_in + 2 * n <= (uintptr_t)c->base + c->bytes &&
+                        c->info.chunk_bytes == 4096 && c->mode != QRC_MODE_STREAM;
+    const bool aligned = ((uintptr_t)d_in & 15) == 0 && ((uintptr_t)d_q & 7) == 0;
+    const qrc_side_info& i = c->info;
+    if (!mapped || !aligned || i.num_sms_measured != (uint32_t)c->num_sms ||
+        i.sms_side0 + i.sms_side1 != (uint32_t)c->num_sms || i.sms_side0 > 128 || i.sms_side1 > 128)
+        return false;
+    if (c->fused_checked == 0) {
+        int coop = 0, per_sm = 0;
+        bool ok = cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, c->device) == cudaSuccess && coop &&
+                  grant_smem((const void*)qrc_k_amax_quant_fused, kFusedSmemBytes) == cudaSuccess &&
+                  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, qrc_k_amax_quant_fused, 1024,
+                                                                kFusedSmemBytes) == cudaSuccess && per_sm >= 1;
+        cudaGetLastError();
+        c->fused_checked = ok ? 1 : -1;
+    }
+    return c->fused_checked > 0;
 }
 
 QRC_API int qrc_amax_quant_e4m3(const uint16_t* d_in, size_t n, uint8_t* d_q, float* d_scale,
@@ -768,10 +1139,24 @@ QRC_API int qrc_amax_quant_e4m3(const uint16_t* d_in, size_t n, uint8_t* d_q, fl
     if (!scope.ok) return QRC_ERR_STATE;
     cudaStream_t s = as_stream(stream);
     float* amax = d_amax ? d_amax : c->d_scalars;
-    const int grid = c->num_sms * c->blocks_per_sm;
-    const size_t smem = launch_smem(c);
     const qrc_u64 n64 = n;
     const qrc_u32 mode = (qrc_u32)c->mode;
+    if (fused_quant_ok(c, d_in, n, d_q)) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(c->num_sms);
+        cfg.blockDim = dim3(1024);
+        cfg.dynamicSmemBytes = kFusedSmemBytes;
+        cfg.stream = s;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeCooperative;
+        attr[0].val.cooperative = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        QRC_CK(cudaLaunchKernelEx(&cfg, qrc_k_amax_quant_fused, d_in, n64, d_q, amax, d_scale, c->d_map, mode));
+        return QRC_OK;
+    }
+    const int grid = c->num_sms * c->blocks_per_sm;
+    const size_t smem = launch_smem(c);
     switch (c->threads) {
         case 1024: QRC_CK(allow_smem<1024>(smem)); QRC_CK(launch(c, qrc_k_amax_bf16<1024>, grid, 1024, smem, s, d_in, n64, c->d_map, amax, d_scale, mode)); break;
         case 512:  QRC_CK(allow_smem<512>(smem)); QRC_CK(launch(c, qrc_k_amax_bf16<512>, grid, 512, smem, s, d_in, n64, c->d_map, amax, d_scale, mode)); break;
@@ -788,6 +1173,20 @@ QRC_API int qrc_amax_quant_e4m3(const uint16_t* d_in, size_t n, uint8_t* d_q, fl
                       c->d_map, mode));
     else if (n)
         QRC_CK(launch(c, qrc_k_quant_e4m3, c->num_sms * 2, 512, 0, s, d_in, n64, d_q, (const float*)d_scale));
+    return QRC_OK;
+}
+
+QRC_API int qrc_debug_quant_launches(qrc_ctx* c, const uint16_t* d_in, size_t n, const uint8_t* d_q) {
+    if (!c) return QRC_ERR_INVALID;
+    DeviceScope scope(c->device);
+    if (!scope.ok) return QRC_ERR_STATE;
+    if (!n) return 1;
+    return fused_quant_ok(c, d_in, n, d_q) ? 1 : 2;
+}
+
+QRC_API int qrc_ctx_debug_quant_fused(qrc_ctx* c, int enable) {
+    if (!c) return QRC_ERR_INVALID;
+    c->quant_fused = enable ? 1 : 0;
     return QRC_OK;
 }
 
@@ -910,6 +1309,30 @@ QRC_API int qrc_debug_cvt_e4m3(const float* d_in, size_t n, uint8_t* d_out, void
     return QRC_OK;
 }
 
+QRC_API int qrc_debug_read_stream(const void* d_in, size_t bytes, int depth, int threads, int blocks_per_sm,
+                                  uint32_t* d_sink, void* stream) {
+    if ((bytes && !d_in) || !d_sink || ((uintptr_t)d_in & 15)) return QRC_ERR_INVALID;
+    int dev = 0, sms = 0;
+    QRC_CK(cudaGetDevice(&dev));
+    QRC_CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    const qrc_u64 nv = bytes / 16;
+    const int grid = sms * blocks_per_sm;
+    cudaStream_t s = as_stream(stream);
+    const uint4* p = (const uint4*)d_in;
+    if (depth == 8 && threads == 1024 && blocks_per_sm == 1)
+        qrc_k_read_stream<8, 1024, 1><<<grid, 1024, 0, s>>>(p, nv, d_sink);
+    else if (depth == 4 && threads == 1024 && blocks_per_sm == 2)
+        qrc_k_read_stream<4, 1024, 2><<<grid, 1024, 0, s>>>(p, nv, d_sink);
+    else if (depth == 16 && threads == 512 && blocks_per_sm == 1)
+        qrc_k_read_stream<16, 512, 1><<<grid, 512, 0, s>>>(p, nv, d_sink);
+    else if (depth == 32 && threads == 256 && blocks_per_sm == 1)
+        qrc_k_read_stream<32, 256, 1><<<grid, 256, 0, s>>>(p, nv, d_sink);
+    else
+        return QRC_ERR_INVALID;
+    QRC_CK(cudaGetLastError());
+    return QRC_OK;
+}
+
 QRC_API void* qrc_ctx_map_device_ptr(const qrc_ctx* c) { return c ? (void*)c->d_map : nullptr; }
 
 QRC_API int qrc_ctx_debug_quant_side_aware(qrc_ctx* c, int enable) {
@@ -957,7 +1380,8 @@ struct Vmm {
     }
 };
 constexpr size_t kVmmPage = 2ull << 20;
-constexpr int kVmmRounds = 8;
+constexpr int kVmmRounds = 8;                 // probe rounds, plus one per kVmmMaxProbe pages of input
+constexpr size_t kVmmMaxProbe = 8192;         // candidate pages per round (16 GiB held at most)
 
 std::vector<qrc_u32> read_words(const qrc_ctx* c, size_t first, size_t n) {
     std::vector<qrc_u32> w(n);
@@ -1026,14 +1450,18 @@ QRC_API int qrc_alloc_like(qrc_vmm_buf** out, void** d_ptr, const qrc_ctx* like)
     size_t need[2] = {0, 0};
     for (size_t p = 0; p < P; p++) need[want[p]]++;
     int rc = QRC_OK;
-    for (int round = 0; round < kVmmRounds && (have[0].size() < need[0] || have[1].size() < need[1]); round++) {
+    const int rounds = kVmmRounds + (int)(P / kVmmMaxProbe);
+    for (int round = 0; round < rounds && (have[0].size() < need[0] || have[1].size() < need[1]); round++) {
         const size_t short0 = need[0] > have[0].size() ? need[0] - have[0].size() : 0;
         const size_t short1 = need[1] > have[1].size() ? need[1] - have[1].size() : 0;
-        const size_t K = 2 * (short0 > short1 ? short0 : short1) + 4;
+        size_t K = 2 * (short0 > short1 ? short0 : short1) + 4;
+        if (K > kVmmMaxProbe) K = kVmmMaxProbe;
         std::vector<CUmemGenericAllocationHandle> batch;
         std::vector<char> kept;
         CUdeviceptr sva = 0;
+        size_t mapped = 0;                                // slots [0, mapped) of sva hold a page
         bool ok = d.reserve(&sva, K * kVmmPage, kVmmPage, 0, 0) == CUDA_SUCCESS;
+        if (!ok) sva = 0;
         for (size_t i = 0; ok && i < K; i++) {
             CUmemGenericAllocationHandle h;
             ok = d.create(&h, kVmmPage, &prop, 0) == CUDA_SUCCESS;
@@ -1041,6 +1469,7 @@ QRC_API int qrc_alloc_like(qrc_vmm_buf** out, void** d_ptr, const qrc_ctx* like)
                 batch.push_back(h);
                 kept.push_back(0);
                 ok = d.map(sva + i * kVmmPage, kVmmPage, 0, h, 0) == CUDA_SUCCESS;
+                if (ok) mapped = i + 1;
             }
         }
         ok = ok && d.access(sva, K * kVmmPage, &acc, 1) == CUDA_SUCCESS;
@@ -1063,7 +1492,10 @@ QRC_API int qrc_alloc_like(qrc_vmm_buf** out, void** d_ptr, const qrc_ctx* like)
         }
         if (probe) qrc_ctx_destroy(probe);
         cudaDeviceSynchronize();
-        if (sva) { d.unmap(sva, K * kVmmPage); d.addrfree(sva, K * kVmmPage); }
+        if (sva) {
+            if (mapped) d.unmap(sva, mapped * kVmmPage);
+            d.addrfree(sva, K * kVmmPage);
+        }
         for (size_t i = 0; i < batch.size(); i++) if (!kept[i]) d.release(batch[i]);
         if (!ok) { rc = QRC_ERR_CUDA; break; }
     }
@@ -1071,18 +1503,24 @@ QRC_API int qrc_alloc_like(qrc_vmm_buf** out, void** d_ptr, const qrc_ctx* like)
     if (rc == QRC_OK) {
         b->va_bytes = P * kVmmPage;
         bool ok = d.reserve(&b->va, b->va_bytes, kVmmPage, 0, 0) == CUDA_SUCCESS;
+        if (!ok) b->va = 0;
         size_t taken[2] = {0, 0};
         for (size_t p = 0; ok && p < P; p++) {
             const CUmemGenericAllocationHandle h = have[want[p]][taken[want[p]]++];
             ok = d.map(b->va + p * kVmmPage, kVmmPage, 0, h, 0) == CUDA_SUCCESS;
             if (ok) b->pages.push_back(h);
+            else d.release(h);                              // taken but not mapped
         }
         ok = ok && d.access(b->va, b->va_bytes, &acc, 1) == CUDA_SUCCESS;
-        // pages not mapped (none, when all went well) go back
+        // pages not taken (none, when all went well) go back
         for (int s = 0; s < 2; s++)
             for (size_t i = taken[s]; i < have[s].size(); i++) d.release(have[s][i]);
         if (!ok) {
-            if (b->va) { d.unmap(b->va, b->va_bytes); d.addrfree(b->va, b->va_bytes); b->va = 0; }
+            if (b->va) {
+                if (!b->pages.empty()) d.unmap(b->va, b->pages.size() * kVmmPage);
+                d.addrfree(b->va, b->va_bytes);
+                b->va = 0;
+            }
             vmm_drop(d, b->pages);
             rc = QRC_ERR_CUDA;
         }
@@ -1106,7 +1544,9 @@ QRC_API int qrc_copy_f32(const float* d_x, float* d_y, size_t n, qrc_ctx* c, voi
                         (uintptr_t)d_x + 4 * n <= (uintptr_t)c->base + c->bytes && c->info.chunk_bytes == 4096;
     const bool aligned = ((uintptr_t)d_x & 15) == 0 && ((uintptr_t)d_y & 15) == 0;
     const bool apart = (uintptr_t)d_y >= (uintptr_t)d_x + 4 * n || (uintptr_t)d_x >= (uintptr_t)d_y + 4 * n;
-    if (mapped && aligned && apart && c->mode != QRC_MODE_STREAM)
+    if (d_x == d_y) return QRC_OK;                       // copying a range onto itself changes nothing
+    if (!apart) return QRC_ERR_INVALID;                 // partial overlap has no defined result
+    if (mapped && aligned && c->mode != QRC_MODE_STREAM)
         QRC_CK(launch(c, qrc_k_copy_f32_sa, c->num_sms, 1024, 0, s, d_x, (qrc_u64)n, d_y, c->d_map,
                       (qrc_u32)c->mode));
     else

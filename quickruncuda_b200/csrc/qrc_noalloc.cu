@@ -24,13 +24,16 @@
 namespace {
 
 // Scratch size: the map header plus one bit per 2 MiB page for up to 32768
-// pages, i.e. inputs spanning at most 64 GiB.  20 KiB per device.
+// pages, i.e. inputs spanning at most 64 GiB.  36 KiB per device.
 constexpr size_t kNoallocPageWords = qrc::kDefaultPageWords;
 constexpr size_t kNoallocWords = qrc::O_PAGE_BITS + kNoallocPageWords;
 constexpr uint64_t kNoallocMaxPages = (uint64_t)kNoallocPageWords * 32;
 
 // Per-device state: the device address of the scratch array (found once per
 // device with cudaGetSymbolAddress) and the input range its side map describes.
+// The address belongs to the device's primary context as it was at set-up:
+// after cudaDeviceReset the entry point must not be used again in the same
+// process (the array would be a different allocation).
 struct NoallocDevice {
     bool ready = false;
     qrc_u32* scratch = nullptr;
@@ -88,7 +91,10 @@ QRC_API int qrc_absmax_f32_noalloc(const float* d_in, size_t n, float* d_out, vo
     }
     if (d.mapped_base != a || d.mapped_bytes != bytes) {
         // New input range: clear the whole array (map, queues, ticket and
-        // accumulator must start at zero) and rediscover for this range.
+        // finish slots must start at zero) and rediscover for this range.
+        // The range is recorded only once both are queued, so a failure here
+        // makes the next call start over instead of trusting a cleared map.
+        d.mapped_base = d.mapped_bytes = 0;
         QRC_NA_CK(cudaMemsetAsync(d.scratch, 0, kNoallocWords * sizeof(qrc_u32), s));
         if (n) qrc_k_noalloc_discover<<<d.num_sms, 1024, 0, s>>>(d_in, bytes, d.scratch);
         QRC_NA_CK(cudaGetLastError());

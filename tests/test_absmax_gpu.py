@@ -230,6 +230,46 @@ def test_host_buffer_entry_point(cuda, qrc, oracle):
         pinned = torch.from_numpy(x).pin_memory()
         assert ctx.absmax_host(pinned) == 7.5
         assert ctx.absmax_host(x[:1000]) == oracle.absmax(x[:1000])
+        assert ctx.absmax_host(x[:0]) == 0.0
+
+
+def test_host_buffer_chunks_and_boundaries(cuda, qrc, oracle):
+    """The host path copies 64 MiB chunks (16 Mi floats) and reduces each as
+    it lands: the maximum must survive at every chunk edge, in a ragged last
+    chunk, and after the staging was reserved larger than the input."""
+    import torch
+    from quickruncuda_b200 import _native as nat
+    chunk = 16 * MIB
+    n = 4 * chunk + 12345
+    x = torch.from_numpy(oracle.uniform(6, n)).pin_memory()
+    with qrc.SideAwareContext(device=0) as ctx:
+        nat.check(ctx.lib, "qrc_host_reserve", ctx.lib.qrc_host_reserve(ctx.handle, n + chunk))
+        for pos in (0, chunk - 1, chunk, 3 * chunk + 7, n - 1):
+            x[pos] = -9.25
+            got = ctx.absmax_host(x)
+            assert np.float32(got) == oracle.absmax(x.numpy()) == np.float32(9.25), pos
+            x[pos] = 0.5
+        assert np.float32(ctx.absmax_host(x)) == oracle.absmax(x.numpy())
+        assert np.float32(ctx.absmax_host(x[:chunk + 3])) == oracle.absmax(x[:chunk + 3].numpy())
+
+
+def test_read_stream_reads_every_word(cuda, qrc, oracle):
+    """The read-ceiling kernel of the bench: every shape XORs every 32-bit
+    word of the buffer exactly once."""
+    import torch
+    from quickruncuda_b200 import _native as nat
+    lib = nat.load()
+    n = 8 * MIB + 4 * 37
+    x = torch.empty(n, dtype=torch.float32, device=cuda)
+    qrc.fill_uniform(x, seed=12)
+    want = int(np.bitwise_xor.reduce(x.cpu().numpy().view(np.uint32)))
+    sink = torch.zeros(1, dtype=torch.int32, device=cuda)
+    for depth, threads, bps in ((8, 1024, 1), (4, 1024, 2), (16, 512, 1), (32, 256, 1)):
+        sink.zero_()
+        assert lib.qrc_debug_read_stream(x.data_ptr(), 4 * n, depth, threads, bps, sink.data_ptr(), None) == 0
+        torch.cuda.synchronize()
+        assert int(sink.item()) & 0xFFFFFFFF == want, (depth, threads, bps)
+    assert lib.qrc_debug_read_stream(x.data_ptr(), 4 * n, 8, 512, 1, sink.data_ptr(), None) == -1
 
 
 def _cov_expect(addr: int, nbytes: int, unit: int = 2):

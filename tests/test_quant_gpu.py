@@ -134,3 +134,67 @@ def test_side_aware_quant_pass_on_mapped_buffer(cuda, qrc, oracle, mode):
         for _ in range(3):
             q3, _, _ = ctx.amax_quant_e4m3(xb)
         assert np.array_equal(q3.cpu().numpy(), oracle.amax_quant_e4m3(base)[0])
+
+
+@pytest.mark.parametrize("mode", [0, 1, 2])
+def test_fused_single_launch_quant(cuda, qrc, oracle, mode):
+    """The single-launch fused kernel (amax, on-chip stash in tensor and
+    shared memory, grid barrier, quantize): bit-exact against the oracle and
+    the two-launch path on views with heads, tails and sizes below one 64 KiB
+    block, and back to back while the maximum moves."""
+    import torch
+    total = (3 << 22) + 4096 + 40
+    base = oracle.normal_bf16(9, total, sigma=2.0)
+    xb = _bf16_tensor(cuda, base)
+    with qrc.SideAwareContext(xb) as ctx:
+        assert ctx.info["status"] == 0
+        ctx.mode = mode
+        for off, n in [(0, total), (8, total - 8), (32768, 1 << 22), (8, 8191), (0, 8), (24, (1 << 21) + 5),
+                       (8, 40000), (0, 0)]:
+            view = xb[off:off + n]
+            q = torch.empty(n, dtype=torch.uint8, device=cuda)
+            assert ctx.quant_launches(view, q) == 1
+            q1, s1, a1 = ctx.amax_quant_e4m3(view, q=q)
+            qo, so = oracle.amax_quant_e4m3(base[off:off + n])
+            assert np.float32(s1.item()) == so, (mode, off, n)
+            assert np.array_equal(q1.cpu().numpy(), qo), (mode, off, n)
+            ctx.set_quant_fused(False)
+            if n:
+                assert ctx.quant_launches(view, q) == 2
+            q2, s2, a2 = ctx.amax_quant_e4m3(view)
+            ctx.set_quant_fused(True)
+            assert torch.equal(q1, q2) and s1.item() == s2.item() and _f32_bits(a1) == _f32_bits(a2)
+        for i in range(4):                           # back to back; the maximum moves every launch
+            pos = [5, total // 2 + 3, total - 1, 70000][i]
+            val = [0x4300, 0xC380, 0x4360, 0xC3C0][i]             # 128, -256, 224, -384
+            saved = int(base[pos])
+            base[pos] = val
+            xb[pos] = int(np.array([val], np.uint16).view(np.int16)[0])
+            q4, s4, a4 = ctx.amax_quant_e4m3(xb)
+            qo, so = oracle.amax_quant_e4m3(base)
+            assert np.float32(s4.item()) == so and np.array_equal(q4.cpu().numpy(), qo), i
+            base[pos] = saved
+            xb[pos] = int(np.array([saved], np.uint16).view(np.int16)[0])
+        assert int(ctx.read_map(128)[99]) == 0      # no bounded wait gave up
+
+
+def test_fused_quant_special_values_on_mapped_buffer(cuda, qrc, oracle):
+    """NaN, infinities, -0 and denormals through the fused kernel."""
+    import torch
+    n = (1 << 21) + 48
+    base = oracle.normal_bf16(10, n, sigma=2.0)
+    xb = _bf16_tensor(cuda, base)
+    with qrc.SideAwareContext(xb) as ctx:
+        for vals in ([0x7FC0, 0xFFC0, 0x8000, 0x0001], [0x7F80, 0xFF80, 0x8001], [0x0000]):
+            b = base.copy()
+            idx = np.arange(0, n, 997)[: 64 * len(vals)]
+            b[idx] = np.resize(np.array(vals, np.uint16), idx.size)
+            if vals == [0x0000]:
+                b[:] = 0
+            xb.copy_(torch.from_numpy(b.view(np.int16)))
+            assert ctx.quant_launches(xb) == 1
+            q, s, a = ctx.amax_quant_e4m3(xb)
+            qo, so = oracle.amax_quant_e4m3(b)
+            assert _f32_bits(s) == int(np.array([so], np.float32).view(np.uint32)[0]), vals
+            assert _f32_bits(a) == int(np.array([oracle.absmax_bf16(b)], np.float32).view(np.uint32)[0]), vals
+            assert np.array_equal(q.cpu().numpy(), qo), vals

@@ -116,3 +116,61 @@ def test_rank_leaving_between_steps_fails_the_next_collective():
     assert res[1] == "left"
     assert res[0].startswith("error after"), res[0]
     assert float(res[0].split()[2].rstrip("s:")) < 30.0
+
+
+def _max_allreduce_worker(rank, world, port, scenario, result_q):
+    """MaxAllReduce on gloo ranks: `leave` (rank 1 announces it left after one
+    step) or `stall` (rank 1 stays alive but skips the second collective)."""
+    from datetime import timedelta
+    from quickruncuda_b200.sharded import MaxAllReduce, PeerLost
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=30))
+    mar = MaxAllReduce(timeout_s=2.0)
+    t = torch.tensor([float(rank + 1)])
+    mar.enqueue(t)
+    mar.wait_all()
+    ok = t.item() == float(world)
+    if rank == 1:
+        if scenario == "leave":
+            mar.leave()
+        result_q.put((rank, ("stepped", ok)))
+        if scenario == "stall":
+            time.sleep(6.0)
+        result_q.close()
+        result_q.join_thread()
+        os._exit(0)
+    time.sleep(0.5 if scenario == "leave" else 0.0)
+    t0 = time.monotonic()
+    try:
+        mar.enqueue(t)
+        mar.wait_all()
+        result_q.put((rank, ("no failure", ok)))
+    except PeerLost as e:
+        result_q.put((rank, ("lost", ok, time.monotonic() - t0, str(e))))
+    result_q.close()
+    result_q.join_thread()
+    os._exit(0)
+
+
+@pytest.mark.parametrize("scenario", ["leave", "stall"])
+def test_max_allreduce_reports_a_lost_rank_fast(scenario):
+    """A rank that announces it left is reported before the next collective
+    starts; a rank that never joins the collective is reported when the
+    deadline (2 s here) passes, not after the process-group timeout (30 s)."""
+    world = 2
+    ctx = mp.get_context("spawn")
+    rq = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_max_allreduce_worker, args=(r, world, port, scenario, rq)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = dict(rq.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(60)
+    assert res[1] == ("stepped", True), res
+    kind, ok, took, msg = res[0]
+    assert kind == "lost" and ok, res
+    if scenario == "leave":
+        assert took < 1.0 and "left" in msg, res
+    else:
+        assert 1.5 < took < 10.0 and "not complete" in msg, res

@@ -8,7 +8,7 @@ import numpy as np
 import pytest
 
 pytestmark = pytest.mark.gpu
-O_SM_SIDE, O_PAGE_BITS, H_NPAGES = 256, 4096, 7
+O_SM_SIDE, O_PAGE_BITS, H_NPAGES = 256, 8192, 7
 
 
 def _page_bits(m):
@@ -64,5 +64,11 @@ def test_side_aware_copy_is_exact(src, qrc):
     ctx.mode = 0
     ctx.copy(x[3:1003], z[5:1005])                                   # unaligned: the plain copy
     assert torch.equal(x[3:1003], z[5:1005])
+    lib = ctx.lib                                                    # overlap: refused; onto itself: no-op
+    assert lib.qrc_copy_f32(x[0:].data_ptr(), x[8:].data_ptr(), 1000, ctx.handle, None) == -1
+    assert lib.qrc_copy_f32(x[8:].data_ptr(), x[0:].data_ptr(), 1000, ctx.handle, None) == -1
+    before = x[:1000].clone()
+    assert lib.qrc_copy_f32(x.data_ptr(), x.data_ptr(), 1000, ctx.handle, None) == 0
+    assert torch.equal(before, x[:1000])
     del y
     torch.cuda.synchronize()

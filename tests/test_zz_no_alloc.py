@@ -20,7 +20,7 @@ def _bits(t):
     return int(t.detach().cpu().view(torch.int32).item()) & 0xFFFFFFFF
 
 
-def test_noalloc_matches_the_context_entry_point_twice_in_a_row(cuda, qrc, lib):
+def test_noalloc_matches_the_context_entry_point_twice_in_a_row(cuda, qrc, lib, oracle):
     import torch
     n = 37 * (1 << 20) + 3                       # spans 75 pages, odd tail
     x = torch.empty(n, dtype=torch.float32, device=cuda)
@@ -31,6 +31,7 @@ def test_noalloc_matches_the_context_entry_point_twice_in_a_row(cuda, qrc, lib):
     with qrc.SideAwareContext(x) as ctx:         # the existing entry point, with its own scratch
         want = _bits(ctx.absmax(x))
     assert want == 0x40C80000                    # 6.25
+    assert want == oracle.absmax_bits(x.cpu().numpy())   # and the CPU oracle on the host copy
     out = torch.full((2,), -1.0, dtype=torch.float32, device=cuda)
     for k in range(2):                           # two calls in a row on the same buffer
         rc = lib.qrc_absmax_f32_noalloc(x.data_ptr(), n, out[k:].data_ptr(), stream)
@@ -41,6 +42,7 @@ def test_noalloc_matches_the_context_entry_point_twice_in_a_row(cuda, qrc, lib):
     y = x[1000:1000 + (5 << 20)]
     with qrc.SideAwareContext(y) as ctx:
         want_y = _bits(ctx.absmax(y))
+    assert want_y == oracle.absmax_bits(y.cpu().numpy())
     for k in range(2):
         assert lib.qrc_absmax_f32_noalloc(y.data_ptr(), y.numel(), out[k:].data_ptr(), stream) == 0
     torch.cuda.synchronize()
