@@ -170,7 +170,7 @@ int qrc_reduce_f32(const float* d_in, size_t n, int op, void* d_out, qrc_ctx* ct
  * only the buffers it works on, a process held to a fixed memory budget, or
  * code that must avoid the implicit synchronisation cudaMalloc may cause.
  * Neither this call nor anything it calls allocates: no context is needed,
- * and its scratch (side map, work queues, ticket, finish slots; 36 KiB) is a
+ * and its scratch (side map, work queues, ticket, accumulator; 20 KiB) is a
  * fixed array that every GPU loading this library holds until exit.  Runs on
  * the current device, asynchronously on `stream`.
  *   - Limit: the input may span at most 32768 pages of 2 MiB (64 GiB, about

@@ -24,7 +24,7 @@
 namespace {
 
 // Scratch size: the map header plus one bit per 2 MiB page for up to 32768
-// pages, i.e. inputs spanning at most 64 GiB.  36 KiB per device.
+// pages, i.e. inputs spanning at most 64 GiB.  20 KiB per device.
 constexpr size_t kNoallocPageWords = qrc::kDefaultPageWords;
 constexpr size_t kNoallocWords = qrc::O_PAGE_BITS + kNoallocPageWords;
 constexpr uint64_t kNoallocMaxPages = (uint64_t)kNoallocPageWords * 32;
@@ -91,7 +91,7 @@ QRC_API int qrc_absmax_f32_noalloc(const float* d_in, size_t n, float* d_out, vo
     }
     if (d.mapped_base != a || d.mapped_bytes != bytes) {
         // New input range: clear the whole array (map, queues, ticket and
-        // finish slots must start at zero) and rediscover for this range.
+        // accumulator must start at zero) and rediscover for this range.
         // The range is recorded only once both are queued, so a failure here
         // makes the next call start over instead of trusting a cleared map.
         d.mapped_base = d.mapped_bytes = 0;

@@ -14,8 +14,7 @@
 //   A        input floats (the harness allocates it with cuMemAlloc, so it is
 //            2 MiB aligned; any 4-byte aligned pointer works here)
 //   B        side map / scratch, zeroed by the harness before init
-//            (QuickRunCUDA.cpp:461-463); layout below, 36 KiB for inputs up to
-//            64 GiB (8192 words plus one bit per 2 MiB page)
+//            (QuickRunCUDA.cpp:461-463); layout below, about 20 KiB
 //   C        C[0] receives absmax(A) after every `kernel` launch
 //   arg0     number of floats (`-0`)
 //   arg1     read mode (`-1`): 0 side-aware, 1 page bits ignored (the
@@ -123,13 +122,6 @@ constexpr int kMaxSm = 256;
 #ifndef QRC_FINISH
 #define QRC_FINISH 1
 #endif
-//   QRC_SLOT_FINISH  1: operators combined by an unsigned maximum finish
-//                  through per-CTA slots and a relaxed ticket (slot_finish);
-//                  0: every launch uses the reduction-plus-fenced-ticket
-//                  finish (ticket_finish)
-#ifndef QRC_SLOT_FINISH
-#define QRC_SLOT_FINISH 1
-#endif
 //   QRC_SHARES     1: the static and balanced schedules may use static
 //                  per-SM shares (see reduce_run); 0: every pair goes through
 //                  the side queues
@@ -189,9 +181,8 @@ enum : qrc_u32 {
     H_ACC64 = 104,                                 // 8-byte aligned double accumulator (sums), 104..105
     H_XCHG_ERR = 106,                              // a peer's value never arrived (sticky until cleared)
     H_QUANT_TICKET = 107,                          // side-aware quantize pass: CTAs done
-    H_EPOCH = 108,                                 // tag of the last launch (slot finish, share marks)
+    H_EPOCH = 108,                                 // share-mark tag of the last launch with shares
     H_COPY_TICKET = 109,                           // side-aware copy: CTAs done
-    H_SLOT_GRID = 110,                             // grid size of the last slot-finish launch
     H_FUSED_ARRIVE = 111,                          // fused quantize: CTAs past the amax phase
     H_FUSED_DONE = 112,                            // fused quantize: CTAs done (ticket)
     H_FUSED_ERR = 113,                             // fused quantize: a bounded wait gave up, or a share was missing
@@ -203,10 +194,8 @@ enum : qrc_u32 {
     O_PAGE_LAT = 1024,                             // first kDiagPages raw page latencies
     O_CLAIMS = 2048,                               // share marks (launch tags): side * 128 + index within side
     O_TIMELINE = 3072,                             // QRC_TIMELINE: 4 words per CTA, 256 CTAs
-    O_SLOTS = 4096,                                // finish slots: one 64-bit word per CTA, kMaxSlots CTAs
-    O_PAGE_BITS = 8192,                            // one bit per 2 MiB page
+    O_PAGE_BITS = 4096,                            // one bit per 2 MiB page
 };
-constexpr qrc_u32 kMaxSlots = (O_PAGE_BITS - O_SLOTS) / 2;
 
 enum : qrc_u32 {
     ST_OK = 0, ST_TOO_SMALL = 1, ST_NO_SM_SPLIT = 2, ST_NO_HASH = 3, ST_BAD_HASH = 4,
@@ -1057,8 +1046,7 @@ QRC_DEV qrc_u32 dynamic_smem_size() {
 // H_WAIT_ERR, drains its own copies (again bounded) and stops; the launch then
 // publishes NaN instead of a maximum.
 template <class Op>
-QRC_DEV typename Op::Acc bulk_walk(typename Op::Acc acc, SideWalk& w, int S, qrc_u32* map, int lane, int warp,
-                                   bool& failed_out) {
+QRC_DEV typename Op::Acc bulk_walk(typename Op::Acc acc, SideWalk& w, int S, qrc_u32* map, int lane, int warp) {
     extern __shared__ __align__(128) unsigned char qrc_dsmem[];
     const int W = blockDim.x >> 5;
     const qrc_u32 U = w.C < kSlotBytes ? (qrc_u32)w.C : kSlotBytes;   // bytes per copy
@@ -1123,7 +1111,6 @@ QRC_DEV typename Op::Acc bulk_walk(typename Op::Acc acc, SideWalk& w, int S, qrc
         for (int t = 0; t < S; t++)                     // drain this warp's copies, bounded
             if (valid & (1u << t)) mbar_wait_bounded(bars + 8u * t, (parity >> t) & 1u);
     }
-    failed_out = failed;
     return acc;
 }
 
@@ -1217,7 +1204,6 @@ QRC_DEV bool xchg_max_u32(const XchgArgs& x, qrc_u32& r) {
 
 struct FinishMaxU32 {
     typedef qrc_u32 Red;
-    static constexpr bool kSlotFinish = true;      // a value fits a finish slot beside its tag
     QRC_DEV bool exchange(const XchgArgs& x, Red& r) { return xchg_max_u32(x, r); }
     QRC_DEV Red neutral() { return 0u; }
     QRC_DEV Red block(Red v) { return block_max(v); }
@@ -1229,7 +1215,6 @@ struct FinishMaxU32 {
 };
 struct FinishSumF64 {
     typedef double Red;
-    static constexpr bool kSlotFinish = false;     // a double leaves no room for the tag
     QRC_DEV bool exchange(const XchgArgs&, Red&) { return false; }   // not offered for sums
     QRC_DEV Red neutral() { return 0.0; }
     QRC_DEV Red block(Red v) { return block_sum_f64(v); }
@@ -1400,225 +1385,14 @@ QRC_DEV typename Op::Acc read_tail(typename Op::Acc acc, const ChunkMap& w, qrc_
     return acc;
 }
 
-// ---- finish ----------------------------------------------------------------
-
-// Slot word of the slot finish: [63:41] the launch tag folded into
-// 1 .. 2^23 - 1 (never 0, so a cleared slot never matches; consecutive tags
-// differ), [40:32] the share the CTA read (0 none, else 1 + side * 128 +
-// index), [31:0] the CTA's value.  A value of kSlotValueErr says a bounded
-// wait gave up: no key an operator produces reaches it (keys of non-NaN
-// floats stay at or below 0xFF800000).
-constexpr qrc_u32 kSlotValueErr = 0xFFFFFFFFu;
-constexpr long long kSlotWaitCycles = 1ll << 31;   // about one second
-QRC_DEV qrc_u32 slot_tag(qrc_u32 tag) { return 1u + tag % 0x7FFFFFu; }
-
-// Finish with per-CTA slots and a relaxed ticket (see reduce_run).
-// `s_tag`, `s_mark` and `s_shares` are the caller's shared variables; they
-// are read only after this function's first barrier.
-template <class Op>
-QRC_DEV void slot_finish(typename Op::Acc acc, bool failed, qrc_u64 a, qrc_u64 end, qrc_u32 mode, qrc_u32* map,
-                         const Shares& sh, const qrc_u32& s_tag, const qrc_u32& s_prev_grid, const qrc_u32& s_mark,
-                         qrc_u32* s_shares, void* out, float* scale_out, const XchgArgs& xa QRC_CS_PARAM) {
-    typedef typename Op::Finish Fin;
-    qrc_u64* slot = (qrc_u64*)(map + O_SLOTS);
-    const qrc_u32 v = block_max(failed ? kSlotValueErr : Op::to_red(acc));
-    __shared__ int s_last;
-    if (threadIdx.x == 0) {
-        const qrc_u32 code = s_mark ? 1u + (s_mark - O_CLAIMS) : 0u;
-        const qrc_u64 word = ((qrc_u64)slot_tag(s_tag) << 41) | ((qrc_u64)code << 32) | v;
-        asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" :: "l"(slot + blockIdx.x), "l"(word) : "memory");
-        qrc_u32 t;
-        asm volatile("atom.relaxed.gpu.global.inc.u32 %0, [%1], %2;"
-                     : "=r"(t) : "l"(&map[H_RUN_TICKET]), "r"(gridDim.x - 1) : "memory");
-        s_last = (t == gridDim.x - 1);
-    }
-    __syncthreads();
-    if (!s_last) return;
-
-    // ---- last CTA: every slot of this launch, missing shares, publish -------
-    const qrc_u32 want = slot_tag(s_tag);
-    qrc_u32 m = 0u;
-    bool late = false;
-    const long long t0 = clock64();
-    for (qrc_u32 i = threadIdx.x; i < gridDim.x && !late; i += blockDim.x) {
-        qrc_u64 w;
-        for (;;) {
-            asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(w) : "l"(slot + i) : "memory");
-            if ((qrc_u32)(w >> 41) == want) break;           // usually at once; else the store is in flight
-            if (clock64() - t0 > kSlotWaitCycles) { late = true; break; }
-        }
-        if (late) break;
-        const qrc_u32 val = (qrc_u32)w;
-        m = val > m ? val : m;
-        const qrc_u32 code = (qrc_u32)(w >> 32) & 0x1FFu;
-        if (code) atomicOr(&s_shares[(code - 1) >> 5], 1u << ((code - 1) & 31));
-    }
-    m = block_max(late ? kSlotValueErr : m);          // its barriers also publish s_shares
-
-    typename Op::Acc acc2 = Op::zero();
-    bool extra = false;
-    if (sh.on) {
-        // Every thread finds the same first share that no slot reported; the
-        // block reads it, and so on until none is missing.
-        for (;;) {
-            int pick = -1;
-            #pragma unroll 1
-            for (int j = 0; j < 8 && pick < 0; j++) {
-                const qrc_u32 K = sh.sms(j >> 2), k0 = (qrc_u32)(j & 3) * 32u;
-                const qrc_u32 req = K <= k0 ? 0u : (K - k0 >= 32u ? 0xFFFFFFFFu : (1u << (K - k0)) - 1u);
-                const qrc_u32 miss = req & ~s_shares[j];
-                if (miss) pick = 32 * j + __ffs(miss) - 1;
-            }
-            if (pick < 0) break;
-            __syncthreads();                           // everyone has read s_shares
-            if (threadIdx.x == 0) s_shares[pick >> 5] |= 1u << (pick & 31);
-            extra = true;
-            ChunkMap cm;
-            cm.setup(a, end, map, mode);
-            acc2 = read_share<Op>(acc2, cm, sh, pick >> 7, pick & 127,
-                                  share_first_page_word(cm, sh, pick & 127, cm.page_bits[0]) QRC_CS_ARG);
-            __syncthreads();                           // the update is visible
-        }
-#ifdef QRC_CHECKED
-        cov_flush(cs, threadIdx.x & 31, map);
-#endif
-    }
-    const qrc_u32 v2 = extra ? block_max(Op::to_red(acc2)) : 0u;
-    if (threadIdx.x == 0) {
-        qrc_u32 r = m > v2 ? m : v2;
-        // Slots a larger previous grid wrote above this grid go back to 0, so
-        // every slot at or above the grid of the last launch is always clear.
-        for (qrc_u32 i = gridDim.x; i < s_prev_grid && i < kMaxSlots; i++) slot[i] = 0ull;
-        if (s_prev_grid != gridDim.x) map[H_SLOT_GRID] = gridDim.x;
-        map[H_EPOCH] = s_tag;
-        map[H_QUEUE0] = 0u;
-        map[H_QUEUE1] = 0u;
-        // Across GPUs an error value is the maximum, so every rank publishes NaN.
-        bool err = false;
-        if (xa.world > 1 && !Fin::exchange(xa, r)) {
-            err = true;
-            map[H_XCHG_ERR] = 1u;
-        }
-        err |= r == kSlotValueErr;
-        // a bounded wait that gave up leaves no valid result: NaN
-        Op::publish(out, scale_out, r, err);
-#if QRC_TIMELINE
-        qrc_u64 t_fin;
-        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_fin));
-        map[O_TIMELINE + 1023] = (qrc_u32)t_fin;      // end of the launch's last CTA
-#endif
-    }
-}
-
-// Finish with a global reduction and a fenced ticket (sums; grids larger than
-// kMaxSlots).  Share marks say which shares were read.
-template <class Op>
-QRC_DEV void ticket_finish(typename Op::Acc acc, qrc_u64 a, qrc_u64 end, qrc_u32 mode, qrc_u32* map,
-                           const Shares& sh, const qrc_u32& s_tag, const qrc_u32& s_mark,
-                           void* out, float* scale_out, const XchgArgs& xa QRC_CS_PARAM) {
-    typedef typename Op::Finish Fin;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const typename Fin::Red v = Fin::block(Op::to_red(acc));
-    __shared__ int s_last;
-    if (threadIdx.x == 0) {
-        qrc_u32 t;
-        if (Op::kIdempotent && sh.on && s_mark) map[s_mark] = s_tag;   // ordered before the ticket
-#if QRC_FINISH == 1
-        // The block's value goes out as a fire-and-forget reduction; the
-        // ticket increment has release semantics (ordered after it) and
-        // acquire semantics (the last CTA then sees every other CTA's
-        // reduction and share mark).
-        Fin::red(map, v);
-        asm volatile("atom.acq_rel.gpu.global.inc.u32 %0, [%1], %2;"
-                     : "=r"(t) : "l"(&map[H_RUN_TICKET]), "r"(gridDim.x - 1) : "memory");
-#else
-        Fin::red(map, v);
-        __threadfence();
-        t = atomicInc(&map[H_RUN_TICKET], gridDim.x - 1);
-        __threadfence();
-#endif
-        s_last = (t == gridDim.x - 1);
-    }
-    __syncthreads();
-    if (!s_last) return;
-
-    // ---- last CTA: unmarked shares, then publish ---------------------------
-    // Warp 1 takes the accumulator while warp 0 loads the share marks: one
-    // round trip for both (the same warp would stall on the exchange's reply
-    // before issuing the mark loads).  Only a missing share costs more.
-    __shared__ typename Fin::Red s_acc;
-    __shared__ qrc_u32 s_wait_err;
-    __shared__ int s_share;
-    if (threadIdx.x == (blockDim.x > 32 ? 32u : 0u)) {
-        s_acc = Fin::take(map);
-        s_wait_err = __ldcg(&map[H_WAIT_ERR]);
-    }
-    typename Op::Acc acc2 = Op::zero();
-    bool extra = false;
-    if (sh.on) {
-        for (;;) {
-            if (warp == 0) {
-                qrc_u32 mark[8];                  // all 256 marks in one round trip
-                #pragma unroll
-                for (int t = 0; t < 8; t++) mark[t] = __ldcg(&map[O_CLAIMS + 32 * t + lane]);
-                int found = -1;
-                #pragma unroll
-                for (int t = 7; t >= 0; t--) {
-                    const int k = (32 * t + lane) & 127;
-                    const unsigned mk = __ballot_sync(0xFFFFFFFFu, (qrc_u32)k < sh.sms(t >> 2) && mark[t] != s_tag);
-                    if (mk) found = 32 * t + __ffs(mk) - 1;
-                }
-                if (lane == 0) {
-                    s_share = found;
-                    if (found >= 0) map[O_CLAIMS + found] = s_tag;
-                }
-            }
-            __syncthreads();
-            const int pick = s_share;
-            __syncthreads();
-            if (pick < 0) break;
-            extra = true;
-            ChunkMap cm;                      // only when a share was missed
-            cm.setup(a, end, map, mode);
-            acc2 = read_share<Op>(acc2, cm, sh, pick >> 7, pick & 127,
-                                  share_first_page_word(cm, sh, pick & 127, cm.page_bits[0]) QRC_CS_ARG);
-        }
-        if (threadIdx.x == 0) map[H_EPOCH] = s_tag;      // the next launch marks with s_tag + 1
-#ifdef QRC_CHECKED
-        cov_flush(cs, lane, map);
-#endif
-    } else {
-        __syncthreads();
-    }
-    const typename Fin::Red v2 = extra ? Fin::block(Op::to_red(acc2)) : Fin::neutral();
-    if (threadIdx.x == 0) {
-        typename Fin::Red r = Fin::combine(s_acc, v2);
-        map[H_QUEUE0] = 0u;
-        map[H_QUEUE1] = 0u;
-        bool err = s_wait_err != 0u;
-        if (xa.world > 1 && !Fin::exchange(xa, r)) {
-            err = true;
-            map[H_XCHG_ERR] = 1u;
-        }
-        // a bounded wait that gave up leaves no valid result: NaN
-        Op::publish(out, scale_out, r, err);
-#if QRC_TIMELINE
-        qrc_u64 t_fin;
-        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_fin));
-        map[O_TIMELINE + 1023] = (qrc_u32)t_fin;      // end of the launch's last CTA
-#endif
-    }
-}
-
-
 // The reduction over n elements at A (element type given by Op).
 //
 // Side-aware path (modes 0-2), register loads:
 //   * Static shares: discovery gave every SM its side s and a dense index k
 //     among the K_s SMs of that side.  The CTA on SM (s, k) reads the side-s
-//     chunks of its share of pairs [0, R) (see read_share).  No atomics.  R is
-//     every pair (static schedule), or 5/8 of them (balanced schedule,
-//     QRC_STATIC_EIGHTHS).
+//     chunks of its share of pairs [0, R) (see read_share).  No atomics.  The
+//     CTA marks its share with a plain store.  R is every pair (static
+//     schedule), or 5/8 of them (balanced schedule, QRC_STATIC_EIGHTHS).
 //   * Balanced schedule: the pairs past R go in 8-pair blocks through the
 //     side queues, one block per claim by each 256-thread group (read_tail),
 //     so SMs that run slower than the static split assumes (the spread across
@@ -1627,7 +1401,7 @@ QRC_DEV void ticket_finish(typename Op::Acc acc, qrc_u64 a, qrc_u64 end, qrc_u32
 //     is read.
 //   * Queue schedule: no shares; warps take one-pair grabs (SideWalk).
 //   * A maximum does not change when an element is read twice, so two CTAs on
-//     one SM only cost time.  A share nobody read (an SM that got no CTA,
+//     one SM only cost time.  A share nobody marked (an SM that got no CTA,
 //     e.g. a grid smaller than the GPU) is read by the last CTA after the
 //     ticket, before it publishes: every element is still read.
 //   * Shares are used when one CTA fills an SM (1024 threads, or a block with
@@ -1636,24 +1410,6 @@ QRC_DEV void ticket_finish(typename Op::Acc acc, qrc_u64 a, qrc_u64 end, qrc_u32
 //     goes through the side queues (SideWalk).
 // Bulk pipeline (dynamic shared memory for >= 2 slots per warp): queues only.
 // Mode 3: side-agnostic grid-stride stream.
-//
-// Finish, for the operators combined by an unsigned maximum (every one but
-// the sums) on grids of up to kMaxSlots CTAs ("slot finish"):
-//   * each CTA reduces its value over the block and its thread 0 stores one
-//     64-bit word in the CTA's slot: the launch's tag, the share it read and
-//     the value (slot_word), then takes a relaxed ticket;
-//   * the last CTA to take a ticket loads every slot and waits (bounded)
-//     until each holds this launch's tag.  The tag, not a fence, orders the
-//     values before their use: a slot that still holds an older launch's word
-//     is simply read again.  The slots also say which shares were read, so a
-//     missing share is found without a separate mark scan;
-//   * the tag is H_EPOCH + 1, read once by each CTA after the wait on the
-//     previous grid; the last CTA advances H_EPOCH, clears the slots a larger
-//     previous grid left above this grid, and resets the queues, so the next
-//     launch starts clean with no host work.
-// Sums (a double per CTA), and grids larger than kMaxSlots, keep the
-// reduction-plus-fenced-ticket finish: a fire-and-forget red into the map,
-// an acquire-release ticket, and share marks scanned by the last CTA.
 template <class Op>
 QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, void* out, float* scale_out, qrc_u32 mode,
                         XchgArgs xa = XchgArgs{nullptr, nullptr, 0u, 0u, 0u}) {
@@ -1665,30 +1421,20 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, void* out, float
     // which kept them resident where the non-coherent path did not.
     const bool plain = bytes <= (qrc_u64)QRC_PLAIN_MAX_BYTES;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, W = blockDim.x >> 5;
-    const bool slots = QRC_SLOT_FINISH && Fin::kSlotFinish && gridDim.x <= kMaxSlots;
     typename Op::Acc acc = Op::zero();
-    bool failed = false;                             // a bounded wait of this thread gave up
 #ifdef QRC_CHECKED
     CheckState cs{a, end, 0ull, 0ull, map};
 #endif
     qrc_u64 lo, hi;   // body [lo, hi); edges [a, lo) and [hi, end)
     Shares sh;
-    __shared__ qrc_u32 s_tag;                        // this launch's tag (slot finish, share marks)
-    __shared__ qrc_u32 s_prev_grid;                  // grid of the last slot-finish launch
+    __shared__ qrc_u32 s_tag;                        // this launch's share-mark tag (share path)
     __shared__ qrc_u32 s_mark;                       // map word of this CTA's share mark, 0 if none
-    __shared__ qrc_u32 s_shares[8];                  // last CTA: shares the slots report as read
-    if (threadIdx.x < 8) s_shares[threadIdx.x] = 0u;
-    if (threadIdx.x == 0) s_mark = 0u;
     sh.on = false;
     sh.K0 = sh.K1 = 0;
 
     if (mode == MODE_STREAM) {
         // Side-agnostic grid-stride stream over the 16-byte aligned body.
         griddep_wait();
-        if (slots && threadIdx.x == blockDim.x - 32) {
-            s_tag = __ldcg(&map[H_EPOCH]) + 1u;
-            s_prev_grid = __ldcg(&map[H_SLOT_GRID]);
-        }
         lo = (a + 15) & ~15ull; hi = end & ~15ull;
         if (hi <= lo) { lo = end; hi = end; }
         const qrc_u64 nv = (hi - lo) / 16;
@@ -1709,14 +1455,16 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, void* out, float
     } else {
         ChunkMap cm;
         cm.setup(a, end, map, mode);      // reads only the map header, which reductions never write
-        const qrc_u32 word0 = map[O_PAGE_BITS];   // goes out with the header loads
+        // These go out with the header loads (one round trip for all): nothing
+        // that decides whether they are needed may wait for that reply.
+        const qrc_u32 word0 = map[O_PAGE_BITS];
+        const qrc_u32 k0 = map[H_NSIDE0], k1 = map[H_NSIDE1];
         lo = cm.lo; hi = cm.hi;
         const int S = bulk_slots_per_warp(dynamic_smem_size(), W);
         sh.on = QRC_SHARES && cm.aware && S < 2 && cm.C == 4096 && (blockDim.x & 255) == 0 &&
                 blockDim.x <= 1024 && (blockDim.x == 1024 || dynamic_smem_size() > 116u * 1024u) &&
                 sched != SCHED_QUEUE;
         if (sh.on) {
-            const qrc_u32 k0 = map[H_NSIDE0], k1 = map[H_NSIDE1];
             sh.K0 = k0;
             sh.K1 = k1;
             sh.on = k0 > 0 && k1 > 0 && k0 <= 128 && k1 <= 128;
@@ -1728,12 +1476,6 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, void* out, float
         const bool own_share = sh.on && own_k >= 0 && (qrc_u32)own_k < sh.sms(cm.side);
         const qrc_u32 pw0 = own_share ? share_first_page_word(cm, sh, own_k, word0) : 0u;
         griddep_wait();                   // the scratch of the previous launch is reset
-        // The last warp fetches the tag (it alone waits for the reply, when
-        // the finish needs it); the finish writes it, after its barriers.
-        if ((slots || sh.on) && threadIdx.x == blockDim.x - 32) {
-            s_tag = __ldcg(&map[H_EPOCH]) + 1u;
-            s_prev_grid = __ldcg(&map[H_SLOT_GRID]);
-        }
 #if QRC_TIMELINE
         qrc_u64 t_start;
         asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_start));
@@ -1743,10 +1485,15 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, void* out, float
 #endif
         if (sh.on) {
             // The tail's first claim goes out now; only its reply stays live
-            // while the share is read.
+            // while the share is read.  A share's mark holds the tag of the
+            // launch that read it (last launch's tag + 1), so marks need no
+            // reset between launches.
             const bool tail = cm.npairs > sh.R;
             qrc_u32 first = 0;
             if (tail && (threadIdx.x & 255) == 0) first = atomicAdd(&map[cm.side ? H_QUEUE1 : H_QUEUE0], 1u);
+            // The last warp fetches the tag (it alone waits for the reply);
+            // the finish, after its barriers, writes the mark.
+            if (threadIdx.x == blockDim.x - 32) s_tag = __ldcg(&map[H_EPOCH]) + 1u;
             if (threadIdx.x == 0) s_mark = own_share ? O_CLAIMS + 128 * cm.side + own_k : 0u;
             if (own_share) {
                 if constexpr (Op::kIdempotent) {
@@ -1757,9 +1504,7 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, void* out, float
                     // Exactly once: the first CTA to set the mark owns the
                     // share.  Warp 0 waits for the claim; the other warps
                     // read the share into its own accumulator meanwhile, and
-                    // it is dropped if the claim was lost.  A share mark holds
-                    // the tag of the launch that read it, so marks need no
-                    // reset between launches.
+                    // it is dropped if the claim was lost.
                     __shared__ qrc_u32 s_lost;
                     if (threadIdx.x == 0) {
                         const qrc_u32 tag = __ldcg(&map[H_EPOCH]) + 1u;
@@ -1786,7 +1531,7 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, void* out, float
             w.setup(a, end, map, mode);
 #ifndef QRC_CHECKED
             if (S >= 2) {
-                acc = bulk_walk<Op>(acc, w, S, map, lane, warp, failed);
+                acc = bulk_walk<Op>(acc, w, S, map, lane, warp);
             } else
 #endif
             {
@@ -1840,16 +1585,98 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, void* out, float
     cov_flush(cs, lane, map);
 #endif
 
-    if constexpr (Fin::kSlotFinish) {
-        if (slots) {
-            slot_finish<Op>(acc, failed, a, end, mode, map, sh, s_tag, s_prev_grid, s_mark, s_shares, out, scale_out,
-                            xa QRC_CS_ARG);
-            return;
-        }
+    // ---- finish: block value, one global reduction, ticket ----------------
+    const typename Fin::Red v = Fin::block(Op::to_red(acc));
+    __shared__ int s_last;
+    if (threadIdx.x == 0) {
+        qrc_u32 t;
+        if (Op::kIdempotent && sh.on && s_mark) map[s_mark] = s_tag;   // ordered before the ticket
+#if QRC_FINISH == 1
+        // The block's value goes out as a fire-and-forget reduction; the
+        // ticket increment has release semantics (ordered after it) and
+        // acquire semantics (the last CTA then sees every other CTA's
+        // reduction and share mark).
+        Fin::red(map, v);
+        asm volatile("atom.acq_rel.gpu.global.inc.u32 %0, [%1], %2;"
+                     : "=r"(t) : "l"(&map[H_RUN_TICKET]), "r"(gridDim.x - 1) : "memory");
+#else
+        Fin::red(map, v);
+        __threadfence();
+        t = atomicInc(&map[H_RUN_TICKET], gridDim.x - 1);
+        __threadfence();
+#endif
+        s_last = (t == gridDim.x - 1);
     }
-    ticket_finish<Op>(acc, a, end, mode, map, sh, s_tag, s_mark, out, scale_out, xa QRC_CS_ARG);
-}
+    __syncthreads();
+    if (!s_last) return;
 
+    // ---- last CTA: unmarked shares, then publish ---------------------------
+    // Warp 1 takes the accumulator while warp 0 loads the share marks: one
+    // round trip for both (the same warp would stall on the exchange's reply
+    // before issuing the mark loads).  Only a missing share costs more.
+    __shared__ typename Fin::Red s_acc;
+    __shared__ qrc_u32 s_wait_err;
+    __shared__ int s_share;
+    if (threadIdx.x == (blockDim.x > 32 ? 32u : 0u)) {
+        s_acc = Fin::take(map);
+        s_wait_err = __ldcg(&map[H_WAIT_ERR]);
+    }
+    typename Op::Acc acc2 = Op::zero();
+    bool extra = false;
+    if (sh.on) {
+        for (;;) {
+            if (warp == 0) {
+                qrc_u32 mark[8];                  // all 256 marks in one round trip
+                #pragma unroll
+                for (int t = 0; t < 8; t++) mark[t] = __ldcg(&map[O_CLAIMS + 32 * t + lane]);
+                int found = -1;
+                #pragma unroll
+                for (int t = 7; t >= 0; t--) {
+                    const int k = (32 * t + lane) & 127;
+                    const unsigned m = __ballot_sync(0xFFFFFFFFu, (qrc_u32)k < sh.sms(t >> 2) && mark[t] != s_tag);
+                    if (m) found = 32 * t + __ffs(m) - 1;
+                }
+                if (lane == 0) {
+                    s_share = found;
+                    if (found >= 0) map[O_CLAIMS + found] = s_tag;
+                }
+            }
+            __syncthreads();
+            const int pick = s_share;
+            __syncthreads();
+            if (pick < 0) break;
+            extra = true;
+            ChunkMap cm;                      // only when a share was missed
+            cm.setup(a, end, map, mode);
+            acc2 = read_share<Op>(acc2, cm, sh, pick >> 7, pick & 127,
+                                  share_first_page_word(cm, sh, pick & 127, cm.page_bits[0]) QRC_CS_ARG);
+        }
+        if (threadIdx.x == 0) map[H_EPOCH] = s_tag;      // the next launch marks with s_tag + 1
+#ifdef QRC_CHECKED
+        cov_flush(cs, lane, map);
+#endif
+    } else {
+        __syncthreads();
+    }
+    const typename Fin::Red v2 = extra ? Fin::block(Op::to_red(acc2)) : Fin::neutral();
+    if (threadIdx.x == 0) {
+        typename Fin::Red r = Fin::combine(s_acc, v2);
+        map[H_QUEUE0] = 0u;
+        map[H_QUEUE1] = 0u;
+        bool err = s_wait_err != 0u;
+        if (xa.world > 1 && !Fin::exchange(xa, r)) {
+            err = true;
+            map[H_XCHG_ERR] = 1u;
+        }
+        // a bounded wait that gave up leaves no valid result: NaN
+        Op::publish(out, scale_out, r, err);
+#if QRC_TIMELINE
+        qrc_u64 t_fin;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_fin));
+        map[O_TIMELINE + 1023] = (qrc_u32)t_fin;      // end of the launch's last CTA
+#endif
+    }
+}
 
 }  // namespace qrc
 

@@ -8,7 +8,7 @@ import numpy as np
 import pytest
 
 pytestmark = pytest.mark.gpu
-O_SM_SIDE, O_PAGE_BITS, H_NPAGES = 256, 8192, 7
+O_SM_SIDE, O_PAGE_BITS, H_NPAGES = 256, 4096, 7
 
 
 def _page_bits(m):
