@@ -188,7 +188,7 @@ int qrc_reduce_f32(const float* d_in, size_t n, int op, void* d_out, qrc_ctx* ct
 int qrc_absmax_f32_noalloc(const float* d_in, size_t n, float* d_out, void* stream);
 
 /* Same result from a host buffer: copies h_in to a device staging buffer owned
- * by the context in 64 MiB chunks on the context's own copy stream, reduces
+ * by the context in 256 MiB chunks on the context's own copy stream, reduces
  * each chunk on `stream` as soon as it has landed (so the reductions hide
  * under the copies), takes the maximum of the chunk results on the device and
  * copies it to *h_out.  The copies start after the work queued on `stream`
@@ -202,7 +202,7 @@ int qrc_absmax_f32_host(const float* h_in, size_t n, float* h_out, qrc_ctx* ctx,
 /* Sets up the staging of qrc_absmax_f32_host for inputs of up to n floats
  * ahead of time: a device buffer of n floats with its own side map
  * (discovery runs on it, synchronously), a copy stream, one event and one
- * partial-result float per 64 MiB chunk.  A larger n replaces the staging; a
+ * partial-result float per 256 MiB chunk.  A larger n replaces the staging; a
  * smaller one keeps it.  On failure nothing is kept and the next call retries.
  * Replaces: the harness' allocation of A before its first launch
  * (QuickRunCUDA.cpp:360-362). */

@@ -228,14 +228,17 @@ qrc_k_quant_e4m3_sa(const uint16_t* in, qrc_u64 n, uint8_t* q, const float* scal
 //     columns per warp, all 512 columns per CTA) and the third in shared
 //     memory (128 KiB per CTA).  The rest of the blocks are claimed one per
 //     group from the side's queue in increasing order (a side whose queue is
-//     empty helps the other), so slower SMs are absorbed.  The top
+//     empty helps the other), so slower SMs are absorbed; the last 4 * K_s
+//     blocks of a side go out as halves (fused_unit).  The top
 //     QRC_FUSED_L2_MB of the input is read with the default L2 policy and
 //     everything else evict-first, so L2 keeps what was read last.
-//   Grid barrier (bounded).  Every CTA adds its block maximum to the map and
-//     arrives; the last to arrive resets the queues and releases the others.
-//   Phase 2 (quantize).  The stash first (no HBM read), then the claimed
-//     blocks again from the same queues, top-down: the blocks read last in
-//     phase 1, those still in L2, come first.
+//   Grid barrier (bounded).  Every CTA adds its block maximum to the map,
+//     claims its first phase-2 block (the claim needs no amax) and arrives;
+//     all wait until every CTA has arrived.
+//   Phase 2 (quantize).  The claimed blocks again, from a second pair of
+//     queues, top-down: the blocks read last in phase 1, those still in L2,
+//     come first.  Group g quantizes its stash block i after g + 2i claimed
+//     blocks, so at any moment most warps have HBM loads in flight.
 // About 58 MB of a 268 MB input never cross HBM twice.  Edges outside the
 // 64 KiB-aligned body are handled by CTA 0 element by element in both
 // phases.  The last CTA to finish (ticket) publishes amax and scale and
@@ -297,6 +300,22 @@ static __device__ __forceinline__ qrc_u32 fused_second(const qrc::ChunkMap& cm, 
 static __device__ __forceinline__ qrc_u64 fused_addr(qrc_u64 row, qrc_u32 second, int j) {
     return row + ((qrc_u64)j << 13) + ((qrc_u64)((second >> j) & 1u) << 12);
 }
+// Claim units of a side's queue in the fused kernel (blocks [dyn, nbf) of a
+// side with K SMs, nd of them): the first nd - T are whole 64 KiB blocks, then
+// 2T halves (4 pairs each) of the last T = min(4K, nd) blocks in claim order, so the end of each phase balances to half a block.  Sets the
+// block's position in claim order and the half (-1 for a whole block);
+// false when the queue is exhausted.
+static __device__ __forceinline__ bool fused_unit(qrc_u32 cur, qrc_u32 nbf, qrc_u32 dyn, qrc_u32 K, qrc_u32& pos,
+                                                  int& half) {
+    const qrc_u32 nd = nbf - dyn, T = 4u * K < nd ? 4u * K : nd, F = nd - T;
+    if (cur < F) { pos = cur; half = -1; return true; }
+    const qrc_u32 h = cur - F;
+    if (h >= 2u * T) return false;
+    pos = F + (h >> 1);
+    half = (int)(h & 1u);
+    return true;
+}
+
 static __device__ __forceinline__ uint8_t quant_one(uint16_t x, float s) {
     return (uint8_t)(cvt_e4m3x2(0.0f, __fmul_rn(__uint_as_float((qrc_u32)x << 16), s)) & 0xFFu);
 }
@@ -328,6 +347,7 @@ qrc_k_amax_quant_fused(const uint16_t* in, qrc_u64 n, uint8_t* q, float* amax_ou
     const qrc_u32 dyn1 = kFusedStash * 4u * k1 < nbf ? kFusedStash * 4u * k1 : nbf;
     const qrc_u32 own_dyn = own_side ? dyn1 : dyn0;
     const qrc_u32 l2_from = nbf > (qrc_u32)kFusedL2Blocks ? nbf - (qrc_u32)kFusedL2Blocks : 0u;
+
     qrc_u32 pat = 0;
     #pragma unroll
     for (int j = 0; j < 8; j++) pat |= (qrc_u32)parity64(((qrc_u64)j << 13) & cm.mask) << j;
@@ -344,6 +364,13 @@ qrc_k_amax_quant_fused(const uint16_t* in, qrc_u64 n, uint8_t* q, float* amax_ou
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const qrc_u32 tslot = s_taddr + ((qrc_u32)((warp & 3) * 32) << 16) + (qrc_u32)(warp >> 2) * 64u;
     griddep_wait();
+#if QRC_TIMELINE
+    // Diagnostic build: per CTA, %globaltimer (ns, low 32 bits) at the start
+    // of phase 1, the arrival at the barrier, its release and the end of
+    // phase 2, in map words O_TIMELINE + 4 * CTA.
+    qrc_u32 tl0;
+    asm volatile("{\n\t.reg .u64 t;\n\tmov.u64 t, %%globaltimer;\n\tcvt.u32.u64 %0, t;\n\t}" : "=r"(tl0));
+#endif
 
     // ---- phase 1: amax ---------------------------------------------------------
     qrc_u32 acc = 0;                                           // two bf16 lanes of max |x|
@@ -366,8 +393,9 @@ qrc_k_amax_quant_fused(const uint16_t* in, qrc_u64 n, uint8_t* q, float* amax_ou
             for (int j = 0; j < 8; j++) sp[j * 1024] = v[j];
         }
     }
+    int par = 0;                                               // s_claim slot of the group's last read
     {                                                          // the claimed blocks, bottom-up
-        int side = own_side, par = 0;
+        int side = own_side;
         bool stealing = false;
         qrc_u32* queue = &map[side ? H_QUEUE1 : H_QUEUE0];
         if (leader) s_claim[0][g] = atomicAdd(queue, 1u);
@@ -375,8 +403,9 @@ qrc_k_amax_quant_fused(const uint16_t* in, qrc_u64 n, uint8_t* q, float* amax_ou
         qrc_u32 cur = s_claim[0][g];
         for (;;) {
             const qrc_u32 dyn = side ? dyn1 : dyn0;
-            qrc_u32 nxt = 0;
-            if (cur >= nbf - dyn) {
+            qrc_u32 nxt = 0, pos;
+            int half;
+            if (!fused_unit(cur, nbf, side ? dyn1 : dyn0, side ? k1 : k0, pos, half)) {
                 if (stealing) break;
                 stealing = true;
                 side ^= 1;
@@ -384,17 +413,19 @@ qrc_k_amax_quant_fused(const uint16_t* in, qrc_u64 n, uint8_t* q, float* amax_ou
                 if (leader) nxt = atomicAdd(queue, 1u);
             } else {
                 if (leader) nxt = atomicAdd(queue, 1u);
-                const qrc_u32 b = dyn + cur;
+                const qrc_u32 b = dyn + pos;
                 const qrc_u64 base = lo64 + ((qrc_u64)b << 16);
-                const qrc_u32 second = fused_second(cm, base, side, pat);
-                const qrc_u64 row = base + 16ull * t;
+                // a half block is pairs 4*half .. 4*half+3: shift the pattern and the row
+                const int j0 = half < 0 ? 0 : 4 * half, jn = half < 0 ? 8 : 4;
+                const qrc_u32 second = fused_second(cm, base, side, pat) >> j0;
+                const qrc_u64 row = base + 16ull * t + ((qrc_u64)j0 << 13);
                 uint4 v[8];
                 if (b >= l2_from) {
                     #pragma unroll
-                    for (int j = 0; j < 8; j++) v[j] = ld16<1>(fused_addr(row, second, j));
+                    for (int j = 0; j < 8; j++) v[j] = j < jn ? ld16<1>(fused_addr(row, second, j)) : make_uint4(0, 0, 0, 0);
                 } else {
                     #pragma unroll
-                    for (int j = 0; j < 8; j++) v[j] = ld16<2>(fused_addr(row, second, j));
+                    for (int j = 0; j < 8; j++) v[j] = j < jn ? ld16<2>(fused_addr(row, second, j)) : make_uint4(0, 0, 0, 0);
                 }
                 #pragma unroll
                 for (int j = 0; j < 8; j++) acc = OpAbsBF16::step16(acc, v[j]);
@@ -405,6 +436,11 @@ qrc_k_amax_quant_fused(const uint16_t* in, qrc_u64 n, uint8_t* q, float* amax_ou
             cur = s_claim[par][g];
         }
     }
+    // The first phase-2 claim goes out now; its reply is read after the barrier.
+    // It goes into the slot the group read two barriers ago (a lagging thread
+    // may still read the other one).
+    par ^= 1;
+    if (leader) s_claim[par][g] = atomicAdd(&map[own_side ? H_FUSED_Q1 : H_FUSED_Q0], 1u);
     // Edges, element by element: [a, lo64) and [body_end, end), both empty or
     // shorter than 64 KiB (when end <= lo64 the head is the whole input).
     const qrc_u64 head_n = ((lo64 < end ? lo64 : end) - a) >> 1, tail_e = (body_end - a) >> 1;
@@ -414,27 +450,25 @@ qrc_k_amax_quant_fused(const uint16_t* in, qrc_u64 n, uint8_t* q, float* amax_ou
     }
 
     // ---- grid barrier ------------------------------------------------------------
-    // Every CTA adds its maximum and its share bit, then arrives.  The last to
-    // arrive resets the queues for phase 2 and releases the others by arriving
-    // once more (gridDim.x + 1).  Waits are bounded.
+    // Every CTA adds its maximum and its share bit, then arrives; all wait
+    // (bounded) until every CTA has arrived.
     const qrc_u32 v = block_max(OpAbsBF16::to_red(acc));
+#if QRC_TIMELINE
+    qrc_u32 tl1, tl2, tl3;
+    asm volatile("{\n\t.reg .u64 t;\n\tmov.u64 t, %%globaltimer;\n\tcvt.u32.u64 %0, t;\n\t}" : "=r"(tl1));
+#endif
     if (tid == 0) {
         asm volatile("red.relaxed.gpu.global.max.u32 [%0], %1;" :: "l"(&map[H_FUSED_ACC]), "r"(v) : "memory");
         if (has_share) atomicOr(&map[O_FUSED_SHARES + ((qrc_u32)own_side * 128u + (qrc_u32)k) / 32u], 1u << (k & 31));
         qrc_u32 arrived;
         asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(arrived) : "l"(&map[H_FUSED_ARRIVE]) : "memory");
         bool ok = true;
-        if (arrived == gridDim.x - 1) {
-            map[H_QUEUE0] = 0u;
-            map[H_QUEUE1] = 0u;
-            asm volatile("red.release.gpu.global.add.u32 [%0], 1;" :: "l"(&map[H_FUSED_ARRIVE]) : "memory");
-        } else {
+        if (arrived != gridDim.x - 1) {
             const long long t0 = clock64();
             for (;;) {
                 asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(arrived) : "l"(&map[H_FUSED_ARRIVE]) : "memory");
-                if (arrived > gridDim.x) break;
+                if (arrived >= gridDim.x) break;
                 if (clock64() - t0 > kFusedWaitCycles) { ok = false; break; }
-                __nanosleep(64);
             }
         }
         float amax = __int_as_float(0x7FFFFFFF);
@@ -451,12 +485,15 @@ qrc_k_amax_quant_fused(const uint16_t* in, qrc_u64 n, uint8_t* q, float* amax_ou
         s_scale = e4m3_scale_from_amax(amax);
     }
     __syncthreads();
+#if QRC_TIMELINE
+    asm volatile("{\n\t.reg .u64 t;\n\tmov.u64 t, %%globaltimer;\n\tcvt.u32.u64 %0, t;\n\t}" : "=r"(tl2));
+#endif
 
     // ---- phase 2: quantize the claimed blocks top-down, and the stash --------
     // Group g quantizes its stash block i between its claimed blocks, after
-    // g + 4i of them, so at any moment about three quarters of the warps of
-    // an SM have HBM loads in flight while the others work from the chip;
-    // what is left of the stash (a group with fewer claims) follows the claims.
+    // g + 2i of them, so at any moment most warps of an SM have HBM loads in
+    // flight while the others work from the chip; what is left of the stash
+    // (a group with fewer claims) follows the claims.
     if (s_ok) {
         const float sc = s_scale;
         int ns = 0;                                            // stash blocks of this group
@@ -483,33 +520,33 @@ qrc_k_amax_quant_fused(const uint16_t* in, qrc_u64 n, uint8_t* q, float* amax_ou
             }
         };
         int si = 0, done = 0;
-        int side = own_side, par = 0;
+        int side = own_side;
         bool stealing = false;
-        qrc_u32* queue = &map[side ? H_QUEUE1 : H_QUEUE0];
-        if (leader) s_claim[0][g] = atomicAdd(queue, 1u);
-        group_bar(g);
-        qrc_u32 cur = s_claim[0][g];
+        qrc_u32* queue = &map[side ? H_FUSED_Q1 : H_FUSED_Q0];
+        qrc_u32 cur = s_claim[par][g];                         // claimed before the barrier
         for (;;) {
-            const qrc_u32 dyn = side ? dyn1 : dyn0;
-            qrc_u32 nxt = 0;
-            if (cur >= nbf - dyn) {
+            qrc_u32 nxt = 0, pos;
+            int half;
+            if (!fused_unit(cur, nbf, side ? dyn1 : dyn0, side ? k1 : k0, pos, half)) {
                 if (stealing) break;
                 stealing = true;
                 side ^= 1;
-                queue = &map[side ? H_QUEUE1 : H_QUEUE0];
+                queue = &map[side ? H_FUSED_Q1 : H_FUSED_Q0];
                 if (leader) nxt = atomicAdd(queue, 1u);
             } else {
                 if (leader) nxt = atomicAdd(queue, 1u);
-                const qrc_u32 b = nbf - 1 - cur;              // top-down
+                const qrc_u32 b = nbf - 1 - pos;              // top-down
                 const qrc_u64 base = lo64 + ((qrc_u64)b << 16);
-                const qrc_u32 second = fused_second(cm, base, side, pat);
-                const qrc_u64 row = base + 16ull * t;
-                if (si < ns && done == g + 4 * si) stash_block(si++);
+                const int j0 = half < 0 ? 0 : 4 * half, jn = half < 0 ? 8 : 4;
+                const qrc_u32 second = fused_second(cm, base, side, pat) >> j0;
+                const qrc_u64 row = base + 16ull * t + ((qrc_u64)j0 << 13);
+                if (si < ns && done == g + 2 * si) stash_block(si++);
                 uint4 v[8];
                 #pragma unroll
-                for (int j = 0; j < 8; j++) v[j] = ld16<2>(fused_addr(row, second, j));
+                for (int j = 0; j < 8; j++) if (j < jn) v[j] = ld16<2>(fused_addr(row, second, j));
                 #pragma unroll
-                for (int j = 0; j < 8; j++) quant16(v[j], sc, q + ((fused_addr(row, second, j) - a) >> 1));
+                for (int j = 0; j < 8; j++)
+                    if (j < jn) quant16(v[j], sc, q + ((fused_addr(row, second, j) - a) >> 1));
                 done++;
             }
             par ^= 1;
@@ -527,6 +564,13 @@ qrc_k_amax_quant_fused(const uint16_t* in, qrc_u64 n, uint8_t* q, float* amax_ou
     // ---- tensor memory back, then the last CTA publishes and resets -------------
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
+#if QRC_TIMELINE
+    asm volatile("{\n\t.reg .u64 t;\n\tmov.u64 t, %%globaltimer;\n\tcvt.u32.u64 %0, t;\n\t}" : "=r"(tl3));
+    if (tid == 0 && blockIdx.x < 256) {
+        qrc_u32* tl = map + O_TIMELINE + 4 * blockIdx.x;
+        tl[0] = tl0; tl[1] = tl1; tl[2] = tl2; tl[3] = tl3;
+    }
+#endif
     if (warp == 0) {
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" :: "r"(s_taddr) : "memory");
@@ -550,6 +594,8 @@ qrc_k_amax_quant_fused(const uint16_t* in, qrc_u64 n, uint8_t* q, float* amax_ou
         map[H_FUSED_ARRIVE] = 0u;
         map[H_QUEUE0] = 0u;
         map[H_QUEUE1] = 0u;
+        map[H_FUSED_Q0] = 0u;
+        map[H_FUSED_Q1] = 0u;
         for (int w = 0; w < 8; w++) map[O_FUSED_SHARES + w] = 0u;
     }
 }
@@ -1122,7 +1168,7 @@ QRC_API int qrc_absmax_f32_allreduce(const float* d_in, size_t n, float* d_out, 
 // copy stream, and each chunk is reduced on the caller's stream as soon as it
 // has landed, so the reduction hides under the copy of the next chunk; one
 // small kernel then takes the maximum of the per-chunk results.
-constexpr size_t kHostChunkFloats = 16ull << 20;          // 64 MiB: 32 whole 2 MiB pages
+constexpr size_t kHostChunkFloats = 64ull << 20;          // 256 MiB: 128 whole 2 MiB pages
 
 // Maximum of `k` per-chunk results.  An unsigned maximum of the bit patterns:
 // the results are non-negative floats or NaN (a reduction whose bounded wait

@@ -188,6 +188,7 @@ enum : qrc_u32 {
     H_FUSED_ERR = 113,                             // fused quantize: a bounded wait gave up, or a share was missing
     H_FUSED_ACC = 114,                             // fused quantize: amax bits of this launch
     O_FUSED_SHARES = 120,                          // fused quantize: 8 words, shares read this launch
+    H_FUSED_Q0 = 160, H_FUSED_Q1 = 192,            // fused quantize: phase-2 queues (own 128-byte lines)
     O_BITLAT = 128,                                // 21 raw latencies of the mask probes
     O_SM_SIDE = 256,                               // per SM: 0 unknown, else 1 + side + 2 * index within side
     O_SM_LAT = 512,                                // per SM raw anchor latency (cycles)

@@ -234,12 +234,12 @@ def test_host_buffer_entry_point(cuda, qrc, oracle):
 
 
 def test_host_buffer_chunks_and_boundaries(cuda, qrc, oracle):
-    """The host path copies 64 MiB chunks (16 Mi floats) and reduces each as
+    """The host path copies 256 MiB chunks (64 Mi floats) and reduces each as
     it lands: the maximum must survive at every chunk edge, in a ragged last
     chunk, and after the staging was reserved larger than the input."""
     import torch
     from quickruncuda_b200 import _native as nat
-    chunk = 16 * MIB
+    chunk = 64 * MIB
     n = 4 * chunk + 12345
     x = torch.from_numpy(oracle.uniform(6, n)).pin_memory()
     with qrc.SideAwareContext(device=0) as ctx:
