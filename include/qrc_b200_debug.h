@@ -55,7 +55,7 @@ int qrc_ctx_debug_quant_side_aware(struct qrc_ctx* ctx, int enable);
 /* 1 (default): qrc_amax_quant_e4m3 runs the single-launch fused kernel
  * whenever its conditions hold (input inside the context's side-aware
  * buffer, 16-byte aligned input, 8-byte aligned output, every SM labelled by
- * discovery, a cooperative launch of one CTA per SM fits); 0: always the two
+ * discovery, exactly one 1024-thread CTA fits per SM); 0: always the two
  * launches (amax pass, then quantize pass), for comparing the two. */
 int qrc_ctx_debug_quant_fused(struct qrc_ctx* ctx, int enable);
 

@@ -218,8 +218,7 @@ qrc_k_quant_e4m3_sa(const uint16_t* in, qrc_u64 n, uint8_t* q, const float* scal
 
 // ---- single-launch fused amax -> e4m3 --------------------------------------
 //
-// One cooperative launch, one 1024-thread CTA per SM, four 256-thread groups
-// per CTA; every group reads the 4 KiB chunk of its die in each of the 8
+// One launch of one 1024-thread CTA per SM, four 256-thread groups per CTA; every group reads the 4 KiB chunk of its die in each of the 8
 // pairs of a 64 KiB block (128 B per thread), like the reduction's walk.
 //   Phase 1 (amax).  The first 3 * 4 * K_s blocks of side s are shared out
 //     statically: the CTA on SM (s, k) reads blocks k*4 + g + i*4*K_s for
@@ -778,7 +777,6 @@ struct qrc_ctx {
     int quant_side_aware = 1;       // side-aware quantize pass when the input is mapped
     int quant_fused = 1;            // single-launch fused quantize when its conditions hold
     int fused_checked = 0;          // 0 not yet, 1 the fused launch fits this device, -1 it does not
-    int fused_pdl = 0;              // -1: the runtime refused programmatic launch with the cooperative one
     const void* base = nullptr;
     size_t bytes = 0;
     qrc_u32* d_map = nullptr;
@@ -1258,9 +1256,9 @@ QRC_API int qrc_absmax_f32_host(const float* h_in, size_t n, float* h_out, qrc_c
 
 // Whether the single-launch fused quantize can run: the input inside the
 // context's side-aware buffer, vector-aligned, every SM labelled by discovery
-// (each SM gets exactly one CTA of a cooperative launch, so every static
-// share is read once), and a cooperative launch of one 1024-thread CTA per
-// SM with the stash's shared memory fits.
+// (each SM gets exactly one CTA, so every static share is read once), and
+// exactly one 1024-thread CTA with the stash's shared memory fits per SM, so
+// a grid of one CTA per SM is resident at once.
 static bool fused_quant_ok(qrc_ctx* c, const uint16_t* d_in, size_t n, const uint8_t* d_q) {
     if (!c->quant_fused || !n || n > ((size_t)1 << 46)) return false;   // 32-bit block indices in the kernel
     const bool mapped = c->info.status == QRC_SIDE_OK && (uintptr_t)d_in >= (uintptr_t)c->base &&
@@ -1272,11 +1270,10 @@ static bool fused_quant_ok(qrc_ctx* c, const uint16_t* d_in, size_t n, const uin
         i.sms_side0 + i.sms_side1 != (uint32_t)c->num_sms || i.sms_side0 > 128 || i.sms_side1 > 128)
         return false;
     if (c->fused_checked == 0) {
-        int coop = 0, per_sm = 0;
-        bool ok = cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, c->device) == cudaSuccess && coop &&
-                  grant_smem((const void*)qrc_k_amax_quant_fused, kFusedSmemBytes) == cudaSuccess &&
+        int per_sm = 0;
+        bool ok = grant_smem((const void*)qrc_k_amax_quant_fused, kFusedSmemBytes) == cudaSuccess &&
                   cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, qrc_k_amax_quant_fused, 1024,
-                                                                kFusedSmemBytes) == cudaSuccess && per_sm >= 1;
+                                                                kFusedSmemBytes) == cudaSuccess && per_sm == 1;
         cudaGetLastError();
         c->fused_checked = ok ? 1 : -1;
     }
@@ -1293,30 +1290,13 @@ QRC_API int qrc_amax_quant_e4m3(const uint16_t* d_in, size_t n, uint8_t* d_q, fl
     const qrc_u64 n64 = n;
     const qrc_u32 mode = (qrc_u32)c->mode;
     if (fused_quant_ok(c, d_in, n, d_q)) {
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3(c->num_sms);
-        cfg.blockDim = dim3(1024);
-        cfg.dynamicSmemBytes = kFusedSmemBytes;
-        cfg.stream = s;
-        cudaLaunchAttribute attr[2];
-        attr[0].id = cudaLaunchAttributeCooperative;
-        attr[0].val.cooperative = 1;
-        attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-        attr[1].val.programmaticStreamSerializationAllowed = 1;
-        cfg.attrs = attr;
-        // Programmatic dependent launch on top of the cooperative launch
-        // hides the launch gap (the kernel waits for the previous grid before
-        // it touches memory); if the runtime refuses the pair, plain
-        // cooperative launches are used from then on.
-        cfg.numAttrs = (c->overlap && c->fused_pdl >= 0) ? 2 : 1;
-        cudaError_t e = cudaLaunchKernelEx(&cfg, qrc_k_amax_quant_fused, d_in, n64, d_q, amax, d_scale, c->d_map, mode);
-        if (e != cudaSuccess && cfg.numAttrs == 2) {
-            cudaGetLastError();
-            c->fused_pdl = -1;
-            cfg.numAttrs = 1;
-            e = cudaLaunchKernelEx(&cfg, qrc_k_amax_quant_fused, d_in, n64, d_q, amax, d_scale, c->d_map, mode);
-        }
-        QRC_CK(e);
+        // One CTA per SM: fused_quant_ok checked that exactly one fits and that
+        // discovery saw every SM, so all CTAs are resident together (its grid
+        // barrier relies on that; the wait is bounded all the same).  Not a
+        // cooperative launch: the runtime gives those no programmatic
+        // overlap with the previous kernel, which costs about 5 us a launch.
+        QRC_CK(launch(c, qrc_k_amax_quant_fused, c->num_sms, 1024, kFusedSmemBytes, s, d_in, n64, d_q, amax, d_scale,
+                      c->d_map, mode));
         return QRC_OK;
     }
     const int grid = c->num_sms * c->blocks_per_sm;
