@@ -599,6 +599,7 @@ def run_ours(args):
         qscale = torch.empty(1, dtype=torch.float32, device=dev)
         qamax = torch.empty(1, dtype=torch.float32, device=dev)
         with q.SideAwareContext(xq, device=local) as cq:
+            cq.set_overlap(not args.no_overlap)
             for _ in range(3):
                 cq.amax_quant_e4m3(xq, q=qout, scale=qscale, amax=qamax)
             qsteps = max(3, min(args.steps, 300))
