@@ -254,6 +254,14 @@ constexpr long long kFusedWaitCycles = 1ll << 31;          // about one second
 #define QRC_FUSED_L2_MB 96
 #endif
 constexpr qrc_u64 kFusedL2Blocks = (qrc_u64)QRC_FUSED_L2_MB << 4;   // 64 KiB blocks
+// Phase 2: group g quantizes stash block i after QRC_FUSED_STASH_G * g +
+// QRC_FUSED_STASH_I * i of its claimed blocks.
+#ifndef QRC_FUSED_STASH_G
+#define QRC_FUSED_STASH_G 1
+#endif
+#ifndef QRC_FUSED_STASH_I
+#define QRC_FUSED_STASH_I 2
+#endif
 
 static __device__ __forceinline__ void tmem_st_x32(qrc_u32 taddr, const uint4 (&v)[8]) {
     asm volatile("tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
@@ -539,7 +547,7 @@ qrc_k_amax_quant_fused(const uint16_t* in, qrc_u64 n, uint8_t* q, float* amax_ou
                 const int j0 = half < 0 ? 0 : 4 * half, jn = half < 0 ? 8 : 4;
                 const qrc_u32 second = fused_second(cm, base, side, pat) >> j0;
                 const qrc_u64 row = base + 16ull * t + ((qrc_u64)j0 << 13);
-                if (si < ns && done == g + 2 * si) stash_block(si++);
+                if (si < ns && done == QRC_FUSED_STASH_G * g + QRC_FUSED_STASH_I * si) stash_block(si++);
                 uint4 v[8];
                 #pragma unroll
                 for (int j = 0; j < 8; j++) if (j < jn) v[j] = ld16<2>(fused_addr(row, second, j));
