@@ -1178,34 +1178,40 @@ struct XchgArgs {
 };
 constexpr long long kXchgWaitCycles = 1ll << 32;   // ~2 s at 2 GHz
 
-// Thread 0 of the last CTA: max of `r` over all ranks; false on timeout.
-QRC_DEV bool xchg_max_u32(const XchgArgs& x, qrc_u32& r) {
+// Warp 0 of the last CTA, every lane: max of `r` over all ranks; false on
+// timeout.  Lane p (and p + 32) stores this rank's (epoch, value) word into
+// rank p's slot array and polls this rank's slot for rank p, so the N stores
+// and the N polls go out in parallel; the warp then takes the maximum.
+QRC_DEV bool xchg_max_u32(const XchgArgs& x, qrc_u32& r, int lane) {
     const qrc_u32 par = x.epoch & 1u;
     const qrc_u64 word = ((qrc_u64)x.epoch << 32) | r;
-    for (qrc_u32 p = 0; p < x.world; p++) {
+    for (qrc_u32 p = (qrc_u32)lane; p < x.world; p += 32) {
         qrc_u64* dst = x.peers[p] + par * x.world + x.rank;
         asm volatile("st.relaxed.sys.global.u64 [%0], %1;" :: "l"(dst), "l"(word) : "memory");
     }
     const long long t0 = clock64();
     qrc_u32 m = r;
-    for (qrc_u32 q = 0; q < x.world; q++) {
+    bool ok = true;
+    for (qrc_u32 q = (qrc_u32)lane; q < x.world && ok; q += 32) {
         qrc_u64 v;
         for (;;) {
             asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(x.local + par * x.world + q) : "memory");
             if ((qrc_u32)(v >> 32) == x.epoch) break;
-            if (clock64() - t0 > kXchgWaitCycles) return false;
-            __nanosleep(256);
+            if (clock64() - t0 > kXchgWaitCycles) { ok = false; break; }
+            __nanosleep(64);
         }
-        const qrc_u32 val = (qrc_u32)v;
-        m = m > val ? m : val;
+        if (ok) {
+            const qrc_u32 val = (qrc_u32)v;
+            m = m > val ? m : val;
+        }
     }
-    r = m;
-    return true;
+    r = __reduce_max_sync(0xFFFFFFFFu, m);
+    return __all_sync(0xFFFFFFFFu, ok);
 }
 
 struct FinishMaxU32 {
     typedef qrc_u32 Red;
-    QRC_DEV bool exchange(const XchgArgs& x, Red& r) { return xchg_max_u32(x, r); }
+    QRC_DEV bool exchange(const XchgArgs& x, Red& r, int lane) { return xchg_max_u32(x, r, lane); }
     QRC_DEV Red neutral() { return 0u; }
     QRC_DEV Red block(Red v) { return block_max(v); }
     QRC_DEV Red combine(Red a, Red b) { return a > b ? a : b; }
@@ -1216,7 +1222,7 @@ struct FinishMaxU32 {
 };
 struct FinishSumF64 {
     typedef double Red;
-    QRC_DEV bool exchange(const XchgArgs&, Red&) { return false; }   // not offered for sums
+    QRC_DEV bool exchange(const XchgArgs&, Red&, int) { return false; }   // not offered for sums
     QRC_DEV Red neutral() { return 0.0; }
     QRC_DEV Red block(Red v) { return block_sum_f64(v); }
     QRC_DEV Red combine(Red a, Red b) { return a + b; }
@@ -1660,22 +1666,25 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, void* out, float
         __syncthreads();
     }
     const typename Fin::Red v2 = extra ? Fin::block(Op::to_red(acc2)) : Fin::neutral();
-    if (threadIdx.x == 0) {
+    if (warp == 0) {                                  // the whole warp: the cross-GPU exchange uses every lane
         typename Fin::Red r = Fin::combine(s_acc, v2);
-        map[H_QUEUE0] = 0u;
-        map[H_QUEUE1] = 0u;
-        bool err = s_wait_err != 0u;
-        if (xa.world > 1 && !Fin::exchange(xa, r)) {
-            err = true;
-            map[H_XCHG_ERR] = 1u;
-        }
-        // a bounded wait that gave up leaves no valid result: NaN
-        Op::publish(out, scale_out, r, err);
+        const bool xchg_ok = xa.world > 1 ? Fin::exchange(xa, r, lane) : true;
+        if (lane == 0) {
+            map[H_QUEUE0] = 0u;
+            map[H_QUEUE1] = 0u;
+            bool err = s_wait_err != 0u;
+            if (!xchg_ok) {
+                err = true;
+                map[H_XCHG_ERR] = 1u;
+            }
+            // a bounded wait that gave up leaves no valid result: NaN
+            Op::publish(out, scale_out, r, err);
 #if QRC_TIMELINE
-        qrc_u64 t_fin;
-        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_fin));
-        map[O_TIMELINE + 1023] = (qrc_u32)t_fin;      // end of the launch's last CTA
+            qrc_u64 t_fin;
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_fin));
+            map[O_TIMELINE + 1023] = (qrc_u32)t_fin;  // end of the launch's last CTA
 #endif
+        }
     }
 }
 
