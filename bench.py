@@ -524,6 +524,9 @@ def run_ours(args):
             return float(t.item())
 
         ksteps = max(3, min(args.steps, 200))
+        for _ in range(3):                      # the first launch of a kernel also loads it
+            ctx.absmax(x, out=out)
+        torch.cuda.synchronize()
         dist.barrier()
         local_ms = max_over_ranks(timed(lambda: ctx.absmax(x, out=out), ksteps, stream))
 
@@ -541,6 +544,9 @@ def run_ours(args):
         nccl_ms = max_over_ranks(nccl_ms)
         fused_ms = None
         if px is not None:
+            for _ in range(3):
+                px.absmax(x, out)
+            torch.cuda.synchronize()
             dist.barrier()
             fused_ms = max_over_ranks(timed(lambda: px.absmax(x, out), ksteps, stream))
             assert out.item() == OUTLIER
