@@ -107,3 +107,41 @@ def test_unmapped_peer_is_refused(data):
         assert lib.qrc_absmax_f32_allreduce(x.data_ptr(), x.numel(), out.data_ptr(), ctx.handle, h, None) == -5
     finally:
         lib.qrc_xchg_destroy(h)
+
+
+def test_forty_ranks_played_from_host(data):
+    """Rank 3 of 40: the last CTA's warp stores into every peer's slot array
+    and polls its own 40 slots lane by lane (lanes 0..7 take two ranks each),
+    so the maximum posted for any rank, including one polled on the second
+    pass of a lane, reaches the result."""
+    import torch
+    x, ctx = data
+    lib = ctx.lib
+    world, rank = 40, 3
+    h = _xchg(lib, rank, world)
+    peers = torch.zeros((world, 2 * world), dtype=torch.int64, device=x.device)   # stand-ins for peer arrays
+    out = torch.empty(1, dtype=torch.float32, device=x.device)
+    try:
+        for p in range(world):
+            if p != rank:
+                assert lib.qrc_xchg_debug_set_peer_ptr(h, p, peers[p].data_ptr()) == 0
+        for high in (37, 11, 3):                      # rank 37 is lane 5's second slot; 3 is this rank
+            e = lib.qrc_xchg_epoch(h) + 1
+            for p in range(world):
+                if p != rank:
+                    v = 6.0 + (4.0 if p == high else p / 64.0)
+                    bits = int(np.array([v], np.float32).view(np.uint32)[0])
+                    assert lib.qrc_xchg_debug_post(h, p, e, bits) == 0
+            assert lib.qrc_absmax_f32_allreduce(x.data_ptr(), x.numel(), out.data_ptr(), ctx.handle, h, None) == 0
+            want = 10.0 if high != rank else 6.0 + 39 / 64.0
+            assert out.item() == np.float32(want), (high, out.item())
+            torch.cuda.synchronize()
+            par = e & 1                                # this rank's word went into every peer's array
+            words = peers[:, par * world + rank].cpu().numpy().astype(np.uint64)
+            for p in range(world):
+                if p != rank:
+                    assert int(words[p]) >> 32 == e and np.array([int(words[p]) & 0xFFFFFFFF], np.uint32).view(np.float32)[0] == 5.5
+        assert int(ctx.read_map(128)[H_XCHG_ERR]) == 0
+    finally:
+        torch.cuda.synchronize()
+        lib.qrc_xchg_destroy(h)
