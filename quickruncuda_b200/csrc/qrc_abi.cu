@@ -562,6 +562,17 @@ qrc_k_amax_quant_fused(const uint16_t* in, qrc_u64 n, uint8_t* q, float* amax_ou
             cur = s_claim[par][g];
         }
         while (si < ns) stash_block(si++);
+#if QRC_TIMELINE
+        // Diagnostic build: per group, the end of its phase-2 work, its claims
+        // and how many of them came from the other side's queue, in map words
+        // O_PAGE_LAT + 2 * (4 * CTA + group) (discovery's diagnostics area).
+        if (leader && blockIdx.x < 148) {
+            qrc_u32 tg;
+            asm volatile("{\n\t.reg .u64 t;\n\tmov.u64 t, %%globaltimer;\n\tcvt.u32.u64 %0, t;\n\t}" : "=r"(tg));
+            map[O_PAGE_LAT + 2 * (4 * blockIdx.x + g)] = tg;
+            map[O_PAGE_LAT + 2 * (4 * blockIdx.x + g) + 1] = (qrc_u32)done | ((qrc_u32)stealing << 16);
+        }
+#endif
         if (blockIdx.x == 0) {
             for (qrc_u64 e = tid; e < head_n; e += blockDim.x) q[e] = quant_one(in[e], sc);
             for (qrc_u64 e = tail_e + tid; e < n; e += blockDim.x) q[e] = quant_one(in[e], sc);
