@@ -231,9 +231,10 @@ qrc_k_quant_e4m3_sa(const uint16_t* in, qrc_u64 n, uint8_t* q, const float* scal
 //     blocks of a side go out as halves (fused_unit).  The top
 //     QRC_FUSED_L2_MB of the input is read with the default L2 policy and
 //     everything else evict-first, so L2 keeps what was read last.
-//   Grid barrier (bounded).  Every CTA adds its block maximum to the map,
-//     claims its first phase-2 block (the claim needs no amax) and arrives;
-//     all wait until every CTA has arrived.
+//   Grid barrier (bounded).  Every CTA adds its block maximum to the map and
+//     arrives; all wait until every CTA has arrived.  Each group's first
+//     phase-2 block (claimed during phase 1; claims and loads need no amax)
+//     is already loading while it waits.
 //   Phase 2 (quantize).  The claimed blocks again, from a second pair of
 //     queues, top-down: the blocks read last in phase 1, those still in L2,
 //     come first.  Group g quantizes its stash block i after g + 2i claimed
@@ -334,6 +335,7 @@ qrc_k_amax_quant_fused(const uint16_t* in, qrc_u64 n, uint8_t* q, float* amax_ou
     extern __shared__ __align__(128) uint4 s_stash[];          // kFusedSmemIters x 8 x 1024 uint4
     __shared__ qrc_u32 s_taddr;
     __shared__ qrc_u32 s_claim[2][4];
+    __shared__ qrc_u32 s_first2[4];                            // each group's first phase-2 claim
     __shared__ float s_scale;
     __shared__ int s_ok, s_last;
     const int tid = threadIdx.x, warp = tid >> 5, g = tid >> 8, t = tid & 255;
@@ -400,6 +402,9 @@ qrc_k_amax_quant_fused(const uint16_t* in, qrc_u64 n, uint8_t* q, float* amax_ou
             for (int j = 0; j < 8; j++) sp[j * 1024] = v[j];
         }
     }
+    // The group's first phase-2 claim goes out now (it needs no amax); its
+    // reply is read after the group barriers of the loop below.
+    if (leader) s_first2[g] = atomicAdd(&map[own_side ? H_FUSED_Q1 : H_FUSED_Q0], 1u);
     int par = 0;                                               // s_claim slot of the group's last read
     {                                                          // the claimed blocks, bottom-up
         int side = own_side;
@@ -443,11 +448,26 @@ qrc_k_amax_quant_fused(const uint16_t* in, qrc_u64 n, uint8_t* q, float* amax_ou
             cur = s_claim[par][g];
         }
     }
-    // The first phase-2 claim goes out now; its reply is read after the barrier.
-    // It goes into the slot the group read two barriers ago (a lagging thread
-    // may still read the other one).
+    // Phase 2's first block is loaded now, so its loads are in flight across
+    // the barrier; the second claim goes out too.  The claim goes into the
+    // slot the group read two barriers ago (a lagging thread may still read
+    // the other one).
     par ^= 1;
     if (leader) s_claim[par][g] = atomicAdd(&map[own_side ? H_FUSED_Q1 : H_FUSED_Q0], 1u);
+    uint4 pv[8];
+    qrc_u32 pos1;
+    int half1;
+    const bool have1 = fused_unit(s_first2[g], nbf, own_dyn, Ks, pos1, half1);
+    const int pj0 = half1 < 0 ? 0 : 4 * half1, pjn = have1 ? (half1 < 0 ? 8 : 4) : 0;
+    qrc_u64 prow = 0;
+    qrc_u32 psecond = 0;
+    if (have1) {
+        const qrc_u64 base = lo64 + ((qrc_u64)(nbf - 1 - pos1) << 16);   // top-down
+        psecond = fused_second(cm, base, own_side, pat) >> pj0;
+        prow = base + 16ull * t + ((qrc_u64)pj0 << 13);
+        #pragma unroll
+        for (int j = 0; j < 8; j++) if (j < pjn) pv[j] = ld16<2>(fused_addr(prow, psecond, j));
+    }
     // Edges, element by element: [a, lo64) and [body_end, end), both empty or
     // shorter than 64 KiB (when end <= lo64 the head is the whole input).
     const qrc_u64 head_n = ((lo64 < end ? lo64 : end) - a) >> 1, tail_e = (body_end - a) >> 1;
@@ -527,10 +547,17 @@ qrc_k_amax_quant_fused(const uint16_t* in, qrc_u64 n, uint8_t* q, float* amax_ou
             }
         };
         int si = 0, done = 0;
+        if (have1) {                                           // the block loaded before the barrier
+            if (si < ns && done == QRC_FUSED_STASH_G * g + QRC_FUSED_STASH_I * si) stash_block(si++);
+            #pragma unroll
+            for (int j = 0; j < 8; j++)
+                if (j < pjn) quant16(pv[j], sc, q + ((fused_addr(prow, psecond, j) - a) >> 1));
+            done++;
+        }
         int side = own_side;
         bool stealing = false;
         qrc_u32* queue = &map[side ? H_FUSED_Q1 : H_FUSED_Q0];
-        qrc_u32 cur = s_claim[par][g];                         // claimed before the barrier
+        qrc_u32 cur = s_claim[par][g];                         // the second claim, made before the barrier
         for (;;) {
             qrc_u32 nxt = 0, pos;
             int half;
