@@ -42,6 +42,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import threading
 import time
 from pathlib import Path
@@ -414,8 +415,9 @@ def reference_kernel_leg(n, local, ours_gbs):
     for name, extra in (("reference_kernel_harness", ["--cubin", str(REF_CUBIN)]),
                         ("our_kernel_file_harness", [str(KERNEL_FILE)])):
         try:
-            p = subprocess.run([str(HARNESS), *common, *extra], capture_output=True, text=True, timeout=300,
-                               cwd=str(ROOT / "gpurun_out") if (ROOT / "gpurun_out").is_dir() else None)
+            with tempfile.TemporaryDirectory(prefix="qrc_harness_") as work:    # the harness writes output.cubin there
+                p = subprocess.run([str(HARNESS), *common, *extra], capture_output=True, text=True, timeout=300,
+                                   cwd=work)
             d = json.loads(p.stdout.strip().splitlines()[-1])
             res[name] = {"gbs": round(d["perf"], 1), "us_per_launch": round(1e3 * d["avg_ms"], 2),
                          "c0": d["c0"], "correct": d["c0"] == OUTLIER}

@@ -218,8 +218,9 @@ qrc_k_quant_e4m3_sa(const uint16_t* in, qrc_u64 n, uint8_t* q, const float* scal
 
 // ---- single-launch fused amax -> e4m3 --------------------------------------
 //
-// One launch of one 1024-thread CTA per SM, four 256-thread groups per CTA; every group reads the 4 KiB chunk of its die in each of the 8
-// pairs of a 64 KiB block (128 B per thread), like the reduction's walk.
+// One launch of one 1024-thread CTA per SM, four 256-thread groups per CTA;
+// every group reads the 4 KiB chunk of its die in each of the 8 pairs of a
+// 64 KiB block (128 B per thread), like the reduction's walk.
 //   Phase 1 (amax).  The first 3 * 4 * K_s blocks of side s are shared out
 //     statically: the CTA on SM (s, k) reads blocks k*4 + g + i*4*K_s for
 //     i < kFusedStash with its group g and keeps them on the chip, the first
@@ -276,18 +277,6 @@ static __device__ __forceinline__ void tmem_st_x32(qrc_u32 taddr, const uint4 (&
                     "r"(v[6].x), "r"(v[6].y), "r"(v[6].z), "r"(v[6].w), "r"(v[7].x), "r"(v[7].y), "r"(v[7].z), "r"(v[7].w)
                  : "memory");
 }
-static __device__ __forceinline__ void tmem_ld_x32(qrc_u32 taddr, uint4 (&v)[8]) {
-    asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-                 "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
-                 "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];\n\t"
-                 "tcgen05.wait::ld.sync.aligned;"
-                 : "=r"(v[0].x), "=r"(v[0].y), "=r"(v[0].z), "=r"(v[0].w), "=r"(v[1].x), "=r"(v[1].y), "=r"(v[1].z), "=r"(v[1].w),
-                   "=r"(v[2].x), "=r"(v[2].y), "=r"(v[2].z), "=r"(v[2].w), "=r"(v[3].x), "=r"(v[3].y), "=r"(v[3].z), "=r"(v[3].w),
-                   "=r"(v[4].x), "=r"(v[4].y), "=r"(v[4].z), "=r"(v[4].w), "=r"(v[5].x), "=r"(v[5].y), "=r"(v[5].z), "=r"(v[5].w),
-                   "=r"(v[6].x), "=r"(v[6].y), "=r"(v[6].z), "=r"(v[6].w), "=r"(v[7].x), "=r"(v[7].y), "=r"(v[7].z), "=r"(v[7].w)
-                 : "r"(taddr) : "memory");
-}
-
 static __device__ __forceinline__ void tmem_ld_x8(qrc_u32 taddr, uint4 (&v)[2]) {
     asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];\n\t"
                  "tcgen05.wait::ld.sync.aligned;"
