@@ -212,8 +212,15 @@ int qrc_host_reserve(qrc_ctx* ctx, size_t n);
  *   amax = max |x| (maxNum), *d_scale = 448 / amax (IEEE division; 1 when amax
  *   is 0 or infinite), d_q[i] = e4m3(x[i] * scale) with round-to-nearest-even
  *   and saturation to +-448 (OCP OFP8 E4M3).  d_amax (may be NULL) receives
- *   amax.  Asynchronous.  No reference counterpart: the quantize extends the
- *   reduction of tests/side_aware.cu:216-219 to the quant_infer use case. */
+ *   amax.  Asynchronous.  When d_in_bf16 lies inside the context's
+ *   side-aware buffer (16-byte aligned, d_q 8-byte aligned) and discovery
+ *   labelled every SM, this is one launch of one CTA per SM: the amax pass
+ *   keeps its last blocks in tensor and shared memory across a bounded grid
+ *   barrier, then quantizes; otherwise two launches (amax, then quantize).
+ *   Both give the same bytes.  If the one-launch path's barrier wait gives up
+ *   (about 1 s), amax is NaN, scale 1 and d_q is not written.
+ *   No reference counterpart: the quantize extends the reduction of
+ *   tests/side_aware.cu:216-219 to the quant_infer use case. */
 int qrc_amax_quant_e4m3(const uint16_t* d_in_bf16, size_t n, uint8_t* d_q, float* d_scale,
                         float* d_amax, qrc_ctx* ctx, void* stream);
 
