@@ -218,7 +218,7 @@ int qrc_host_reserve(qrc_ctx* ctx, size_t n);
  *   keeps its last blocks in tensor and shared memory across a bounded grid
  *   barrier, then quantizes; otherwise two launches (amax, then quantize).
  *   Both give the same bytes.  If the one-launch path's barrier wait gives up
- *   (about 1 s), amax is NaN, scale 1 and d_q is not written.
+ *   (about 1 s), amax is NaN and scale 1, and d_q holds no valid result.
  *   No reference counterpart: the quantize extends the reduction of
  *   tests/side_aware.cu:216-219 to the quant_infer use case. */
 int qrc_amax_quant_e4m3(const uint16_t* d_in_bf16, size_t n, uint8_t* d_q, float* d_scale,
