@@ -173,7 +173,7 @@ class ClockSampler:
                0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown", 0x2: "applications_clocks_setting",
                0x10: "sync_boost", 0x100: "display_clock_setting"}
 
-    def __init__(self, index: int, period_s: float = 0.002):
+    def __init__(self, index: int, period_s: float = 0.001):
         self.ok = False
         self.samples = []
         self.period = period_s
