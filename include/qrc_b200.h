@@ -52,8 +52,9 @@ enum qrc_mode {
     /* Work schedule, OR-ed into a side-aware mode (default: chosen by size). */
     QRC_SCHED_STATIC = 0x10,        /* every SM reads a fixed share: no atomics */
     QRC_SCHED_QUEUE = 0x20,         /* warps take one-pair grabs from per-side queues */
-    QRC_SCHED_BALANCED = 0x30       /* static shares for 5/8 of the input, the rest
-                                       claimed in 64 KiB blocks from per-side queues */
+    QRC_SCHED_BALANCED = 0x30       /* static shares for 5/8 of the input (1/8 above
+                                       1 GiB), the rest claimed in 64 KiB blocks from
+                                       per-side queues */
 };
 
 /* Discovery status (qrc_side_info.status). */

@@ -143,7 +143,7 @@ class SideAwareContext:
     def schedule(self, name: str) -> None:
         """'auto' (by size), 'static' (fixed per-SM shares), 'queue' (one-pair
         grabs from per-side queues) or 'balanced' (static shares for 5/8 of
-        the input, the rest claimed in 64 KiB blocks)."""
+        the input, 1/8 above 1 GiB, the rest claimed in 64 KiB blocks)."""
         sched = nat.SCHED_NAMES[name]
         nat.check(self.lib, "qrc_ctx_set_mode",
                   self.lib.qrc_ctx_set_mode(self.handle, self._mode | sched))

@@ -60,9 +60,10 @@
 //     each, so every byte is read exactly once whatever the map says -- the
 //     map only decides locality, never coverage;
 //   * work goes out as static per-SM shares of 64 KiB blocks (inputs up to
-//     256 MiB), as static shares for 5/8 with the rest claimed block by
-//     block from a per-side queue (larger inputs), or as one-pair grabs from
-//     the per-side queues (launch shapes the shares cannot serve);
+//     256 MiB), as static shares for 5/8 (1/8 above 1 GiB) with the rest
+//     claimed block by block from a per-side queue (larger inputs), or as
+//     one-pair grabs from the per-side queues (launch shapes the shares
+//     cannot serve);
 //   * per element max(acc, |x|) with IEEE maxNum semantics written in PTX
 //     (NaN never wins, -0 -> +0, denormals kept even under -use_fast_math);
 //     QRC_PLUGIN_OP selects max, min, sum or sum of squares instead;
@@ -132,8 +133,17 @@ constexpr int kMaxSm = 256;
 //                  static shares; the rest is claimed block by block from the
 //                  side queues, which absorbs SMs that run slower than their
 //                  share assumes
+//   QRC_STATIC_EIGHTHS_LARGE  the same above QRC_LARGE_PAIRS pairs (1 GiB),
+//                  where a smaller static part measured faster (0.3-1 % at
+//                  4 GB) and below which it measured slower
 #ifndef QRC_STATIC_EIGHTHS
 #define QRC_STATIC_EIGHTHS 5
+#endif
+#ifndef QRC_STATIC_EIGHTHS_LARGE
+#define QRC_STATIC_EIGHTHS_LARGE 1
+#endif
+#ifndef QRC_LARGE_PAIRS
+#define QRC_LARGE_PAIRS 131072
 #endif
 //   QRC_STATIC_MAX_PAIRS  automatic schedule: static shares alone up to this
 //                  many 8 KiB pairs, the balanced schedule above
@@ -145,6 +155,13 @@ constexpr int kMaxSm = 256;
 #endif
 #ifndef QRC_STATIC_MAX_PAIRS
 #define QRC_STATIC_MAX_PAIRS 32768
+#endif
+//   QRC_SM_FIRST_MAX_PAIRS  static shares of up to this many pairs (with no
+//                  queued tail) hand
+//                  consecutive 8-pair blocks to different SMs; larger ones
+//                  give each SM G adjacent blocks (see Shares)
+#ifndef QRC_SM_FIRST_MAX_PAIRS
+#define QRC_SM_FIRST_MAX_PAIRS 16384
 #endif
 //   QRC_ACROSS     1: a warp takes its next 8 chunks together and loads slice k
 //                  of all 8 before slice k+1 (8 chunks in flight, one 512-byte
@@ -1240,14 +1257,26 @@ struct FinishSumF64 {
 // thread t loads bytes 16t..16t+15 of each of the 8 chunks (eight 16-byte
 // loads in flight, all addresses computed on the spot).  Block b of 8 pairs
 // belongs to group b mod (K_s * G) of side s, G = groups per CTA, and group g
-// of the CTA on the SM with index k is group k * G + g, so each SM steps
-// through 8*G adjacent pairs while the K_s SMs of a side sweep one window.
+// of the CTA on the SM with index k is group
+//   * g * K_s + k when the shares are the whole input and R <=
+//     QRC_SM_FIRST_MAX_PAIRS: consecutive blocks go to
+//     different SMs, so a small input spreads over as many SMs as it has
+//     blocks (4 MB: 64 SMs of a side with 32 KiB each, not 16 with 128 KiB)
+//     and the SMs' totals differ by at most one block;
+//   * k * G + g above that, so each SM steps through 8*G adjacent pairs, which
+//     reads faster from DRAM when every SM has many blocks.
+// Either way the K_s SMs of a side sweep one window of K_s * G blocks.
 // Requires 4 KiB chunks (one 16-byte load per thread covers a chunk).
 struct Shares {
     qrc_u64 R;          // pairs [0, R) are shared out statically
     qrc_u32 K0, K1;     // SMs per side
     bool on;
+    bool sm_first;      // group of (k, g) is g * K_s + k, else k * G + g
     QRC_MEMBER qrc_u32 sms(int s) const { return s ? K1 : K0; }
+    // First block of group g of SM k of side s.
+    QRC_MEMBER qrc_u64 first_block(int s, int k, int g) const {
+        return sm_first ? (qrc_u64)g * sms(s) + k : (qrc_u64)k * (blockDim.x >> 8) + g;
+    }
 };
 
 // Page-bit word of 8-pair block b when the share fast path (64 KiB aligned
@@ -1260,20 +1289,21 @@ QRC_DEV qrc_u32 block_page_word(const ChunkMap& w, const Shares& sh, qrc_u64 b) 
 }
 // `word0` is page-bit word 0, loaded with the map header: a share whose first
 // block lies in the first 64 MiB of the mapped buffer needs no second load.
-QRC_DEV qrc_u32 share_first_page_word(const ChunkMap& w, const Shares& sh, int k, qrc_u32 word0) {
-    const qrc_u64 b = (qrc_u64)k * (blockDim.x >> 8) + (threadIdx.x >> 8);
+// The share is that of SM k of side s.
+QRC_DEV qrc_u32 share_first_page_word(const ChunkMap& w, const Shares& sh, int s, int k, qrc_u32 word0) {
+    const qrc_u64 b = sh.first_block(s, k, threadIdx.x >> 8);
     if (!w.use_page_bits || (w.lo & 0xFFFFull) != 0 || (b + 1) * 8 > sh.R) return 0u;
     const qrc_u64 pg = (w.lo + (b << 16) - w.page_base) >> 21;
     return (pg >> 5) == 0 ? word0 : w.page_bits[pg >> 5];
 }
 
-// `pw` is share_first_page_word(w, sh, k).
+// `pw` is share_first_page_word(w, sh, s, k).
 template <class Op, int Kind = QRC_LOAD_KIND>
 QRC_DEV typename Op::Acc read_share(typename Op::Acc acc, const ChunkMap& w, const Shares& sh, int s, int k,
                                     qrc_u32 pw QRC_CS_PARAM) {
     const int G = blockDim.x >> 8, g = threadIdx.x >> 8, t = threadIdx.x & 255;
     const qrc_u64 groups = (qrc_u64)sh.sms(s) * G, npairs = sh.R;
-    qrc_u64 b = (qrc_u64)k * G + g;
+    qrc_u64 b = sh.first_block(s, k, g);
     if ((w.lo & 0xFFFFull) == 0) {
         // Fast path: a block is 64 KiB aligned, so its 8 pairs share one page
         // bit, and pair j's masked-address parity is the block's XOR bit j of
@@ -1399,7 +1429,8 @@ QRC_DEV typename Op::Acc read_tail(typename Op::Acc acc, const ChunkMap& w, qrc_
 //     among the K_s SMs of that side.  The CTA on SM (s, k) reads the side-s
 //     chunks of its share of pairs [0, R) (see read_share).  No atomics.  The
 //     CTA marks its share with a plain store.  R is every pair (static
-//     schedule), or 5/8 of them (balanced schedule, QRC_STATIC_EIGHTHS).
+//     schedule), or 5/8 of them, 1/8 above 1 GiB (balanced schedule,
+//     QRC_STATIC_EIGHTHS, QRC_STATIC_EIGHTHS_LARGE).
 //   * Balanced schedule: the pairs past R go in 8-pair blocks through the
 //     side queues, one block per claim by each 256-thread group (read_tail),
 //     so SMs that run slower than the static split assumes (the spread across
@@ -1437,6 +1468,7 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, void* out, float
     __shared__ qrc_u32 s_tag;                        // this launch's share-mark tag (share path)
     __shared__ qrc_u32 s_mark;                       // map word of this CTA's share mark, 0 if none
     sh.on = false;
+    sh.sm_first = false;
     sh.K0 = sh.K1 = 0;
 
     if (mode == MODE_STREAM) {
@@ -1477,11 +1509,13 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, void* out, float
             sh.on = k0 > 0 && k1 > 0 && k0 <= 128 && k1 <= 128;
             const bool tail = sched == SCHED_BALANCED ||
                               (sched == SCHED_AUTO && cm.npairs > (qrc_u64)QRC_STATIC_MAX_PAIRS);
-            sh.R = tail ? (cm.npairs * QRC_STATIC_EIGHTHS / 8) & ~7ull : cm.npairs;   // whole 8-pair blocks
+            const qrc_u64 eighths = cm.npairs > (qrc_u64)QRC_LARGE_PAIRS ? QRC_STATIC_EIGHTHS_LARGE : QRC_STATIC_EIGHTHS;
+            sh.R = tail ? (cm.npairs * eighths / 8) & ~7ull : cm.npairs;   // whole 8-pair blocks
+            sh.sm_first = !tail && sh.R <= (qrc_u64)QRC_SM_FIRST_MAX_PAIRS;
         }
         const int own_k = cm.sm_index;
         const bool own_share = sh.on && own_k >= 0 && (qrc_u32)own_k < sh.sms(cm.side);
-        const qrc_u32 pw0 = own_share ? share_first_page_word(cm, sh, own_k, word0) : 0u;
+        const qrc_u32 pw0 = own_share ? share_first_page_word(cm, sh, cm.side, own_k, word0) : 0u;
         griddep_wait();                   // the scratch of the previous launch is reset
 #if QRC_TIMELINE
         qrc_u64 t_start;
@@ -1656,7 +1690,7 @@ QRC_DEV void reduce_run(const void* A, qrc_u64 n, qrc_u32* map, void* out, float
             ChunkMap cm;                      // only when a share was missed
             cm.setup(a, end, map, mode);
             acc2 = read_share<Op>(acc2, cm, sh, pick >> 7, pick & 127,
-                                  share_first_page_word(cm, sh, pick & 127, cm.page_bits[0]) QRC_CS_ARG);
+                                  share_first_page_word(cm, sh, pick >> 7, pick & 127, cm.page_bits[0]) QRC_CS_ARG);
         }
         if (threadIdx.x == 0) map[H_EPOCH] = s_tag;      // the next launch marks with s_tag + 1
 #ifdef QRC_CHECKED

@@ -125,3 +125,24 @@ def test_balanced_schedule_covers_every_chunk_once(oracle, npairs, k0, k1, eight
     rng = np.random.default_rng(npairs + eighths)
     covered = _balanced_cover(oracle, npairs, k0, k1, 4, eighths, rng)
     assert np.all(covered == 1)
+
+
+def _first_block(sm_first, K, G, k, g):
+    """Same arithmetic as Shares::first_block."""
+    return g * K + k if sm_first else k * G + g
+
+
+@pytest.mark.parametrize("K", [1, 3, 70, 74, 78])
+@pytest.mark.parametrize("G", [1, 2, 4])
+@pytest.mark.parametrize("sm_first", [False, True])
+def test_share_groups_are_a_bijection_and_sm_first_balances(K, G, sm_first):
+    """Every (SM k, group g) pair starts at a distinct block of [0, K*G), so
+    blocks b, b + K*G, ... cover every block once; with the SM-first order
+    the blocks per SM differ by at most one for every input size."""
+    firsts = sorted(_first_block(sm_first, K, G, k, g) for k in range(K) for g in range(G))
+    assert firsts == list(range(K * G))
+    for nb in (0, 1, 5, 64, K * G - 1, K * G, K * G + 3, 1024, 4096 + 7):
+        per_sm = [sum(len(range(_first_block(sm_first, K, G, k, g), nb, K * G)) for g in range(G))
+                  for k in range(K)]
+        assert sum(per_sm) == nb
+        assert max(per_sm) - min(per_sm) <= (1 if sm_first else G)
