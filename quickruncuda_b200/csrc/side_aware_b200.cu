@@ -149,9 +149,12 @@ constexpr int kMaxSm = 256;
 //                  many 8 KiB pairs, the balanced schedule above
 //   QRC_PLAIN_MAX_BYTES  static shares of inputs up to this size are read
 //                  with plain ld.global.v4 (flavour 0), larger ones with
-//                  QRC_LOAD_KIND
+//                  QRC_LOAD_KIND.  Back to back, plain loads keep much of an
+//                  input up to ~1.1x the 126 MB L2 resident (112-128 MiB:
+//                  11-11.8 TB/s against 7.0-7.3 TB/s; 136 MiB: +2 %); from
+//                  144 MiB on they lose 17-21 % to the non-coherent path
 #ifndef QRC_PLAIN_MAX_BYTES
-#define QRC_PLAIN_MAX_BYTES (96ull << 20)
+#define QRC_PLAIN_MAX_BYTES (136ull << 20)
 #endif
 #ifndef QRC_STATIC_MAX_PAIRS
 #define QRC_STATIC_MAX_PAIRS 32768
