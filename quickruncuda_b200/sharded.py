@@ -2,7 +2,8 @@
 shard with the side-aware kernel, then one single-float max all-reduce.
 
 The reference has no multi-GPU path (QuickRunCUDA.cpp:286 fixes device 0);
-this is the north star's sharded variant.  The exchange is one float per rank.
+this is new: N GPUs, each with its own 1e9-float shard, and one maximum.
+The exchange is one float per rank.
 Two ways carry it:
   * PeerMax: inside the reduction kernel.  The last CTA of each rank stores
     its partial in every rank's exchange slots over NVLink (CUDA IPC
