@@ -99,7 +99,8 @@ def test_kernel_file_under_reference_harness(tmp_path, oracle, seed, mask, n):
 
 @needs_ref
 def test_reference_kernel_under_our_harness(tmp_path, oracle):
-    """The reference kernel on the config-1 input gives the oracle's answer."""
+    """The reference kernel on a 1 Mi-float uniform input with one planted 7.5
+    gives the oracle's answer."""
     n = 1048576
     res = harness_json(["--cubin", REF_CUBIN, "-i", "-p", "-t", "1024", "-A", 4 * n, "-0", n, "-C", 1,
                         "-T", 3, "--fill-a", "uniform:0:7.5"], tmp_path)
