@@ -114,3 +114,32 @@ def test_kernel_file_is_self_contained():
     src = KERNEL_FILE.read_text()
     assert "#include" not in src.split("#ifndef QRC_SIDE_AWARE_B200_CU")[1]
     assert 'extern "C" __global__' in src and "init(" in src and "kernel(" in src
+
+
+def _kernel_define(name):
+    m = re.search(rf"^#define {name} (.+)$", KERNEL_FILE.read_text(), re.M)
+    assert m, name
+    return m.group(1).strip()
+
+
+def test_bench_schedule_label_matches_kernel_threshold():
+    """bench.py labels the automatic schedule by size; its byte threshold is
+    the kernel's QRC_STATIC_MAX_PAIRS 8 KiB pairs."""
+    import sys
+    sys.path.insert(0, str(ROOT))
+    import bench
+    assert bench.STATIC_MAX_BYTES == int(_kernel_define("QRC_STATIC_MAX_PAIRS")) * 8192
+
+
+def test_schedule_thresholds_are_ordered():
+    """SM-first shares stay inside the static-only range, and the 1/8 static
+    part applies only where the balanced schedule runs."""
+    sm_first = int(_kernel_define("QRC_SM_FIRST_MAX_PAIRS"))
+    static_max = int(_kernel_define("QRC_STATIC_MAX_PAIRS"))
+    large = int(_kernel_define("QRC_LARGE_PAIRS"))
+    plain = _kernel_define("QRC_PLAIN_MAX_BYTES")
+    m = re.fullmatch(r"\((\d+)ull << 20\)", plain)
+    assert m, plain
+    assert sm_first <= static_max < large
+    assert int(m.group(1)) << 20 <= static_max * 8192
+    assert 0 <= int(_kernel_define("QRC_STATIC_EIGHTHS_LARGE")) <= int(_kernel_define("QRC_STATIC_EIGHTHS")) <= 8
